@@ -1,0 +1,249 @@
+"""Algebraic FlashAttention forward on B200, behind the reference's signatures.
+
+Drop-in for the forward entry points of src/kernels/pallas_afa.py
+(tasmaikeni13/algebraic-intelligence):
+
+* ``pallas_afa_forward``        -- pallas_afa.py:154-264 (same arguments, same
+                                   ValueError conditions and messages)
+* ``tiled_afa_forward``         -- pallas_afa.py:330-406 (the reference's XLA
+                                   path; same math, so the same kernels)
+* ``pallas_afa``                -- pallas_afa.py:579-612, forward only
+* ``algebraic_flash_attention`` -- pallas_afa.py:695-739; any sequence length,
+                                   handled in-kernel by masking instead of
+                                   padding copies
+* ``afa_decode``                -- no reference counterpart: one query token per
+                                   (batch, head) over a KV cache
+
+Arrays are torch CUDA tensors shaped (batch, heads, sequence, dim); NumPy arrays
+and CPU tensors are accepted and staged through the GPU. ``block_q`` /
+``block_k`` and ``interpret`` are validated like the reference but do not
+change the computation: the B200 kernels tile at 128 x 128 on the tensor cores
+and the result of the additive accumulation does not depend on the tiling
+(the reference's own associativity test, tests/test_pallas_afa.py:207-224).
+"""
+from __future__ import annotations
+
+import ctypes
+import math
+from typing import Optional
+
+import torch
+
+from . import _lib
+from ._tensors import Staged, host_checks_float
+
+__all__ = [
+    "pallas_afa_forward",
+    "tiled_afa_forward",
+    "pallas_afa",
+    "algebraic_flash_attention",
+    "afa_decode",
+]
+
+
+def _sink_ok(sink_omega) -> bool:
+    try:
+        return 0.0 <= float(sink_omega) < float("inf")
+    except (TypeError, ValueError):
+        return False
+
+
+def _launch_fwd(q, k, v, sink_omega, causal, valid_seq_len, return_denominator):
+    st = Staged(q, k, v)
+    q, k, v = st.tensors
+    if not (q.dtype == k.dtype == v.dtype):
+        raise TypeError(f"q, k and v must share a dtype, got {q.dtype}, {k.dtype} and {v.dtype}")
+    code = _lib.dtype_code(q.dtype)
+    b, h, l, d = q.shape
+    out = torch.empty_like(q)
+    den = torch.empty((b, h, l, 1), dtype=_lib.accum_dtype(q.dtype), device=q.device)
+    lib = _lib.load()
+    with torch.cuda.device(q.device):
+        rc = lib.afa_fwd(q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), den.data_ptr(), b, h, l, d, code,
+                         float(sink_omega), int(bool(causal)), int(valid_seq_len or 0), _lib.stream_ptr(q.device))
+    _lib.check(rc, "afa_fwd")
+    if return_denominator:
+        return st.back(out), st.back(den)
+    return st.back(out)
+
+
+def pallas_afa_forward(q, k, v, sink_omega: float = 0.5, causal: bool = False, block_q: int = 128,
+                       block_k: int = 128, valid_seq_len: Optional[int] = None, interpret: Optional[bool] = None,
+                       return_denominator: bool = False):
+    """AFA forward (src/kernels/pallas_afa.py:154-264).
+
+    Returns ``out`` (q's shape and dtype) or ``(out, d_total)`` where
+    ``d_total`` = row sum + sink, shape (B, H, L, 1), float32 (float64 for
+    float64 inputs). bfloat16 inputs with head_dim 64 or 128 run on the tcgen05
+    tensor cores; float32 / float64 on the CUDA cores at full precision
+    (the reference's Precision.HIGHEST, pallas_afa.py:224-228).
+    """
+    del interpret  # there is one execution path: the GPU kernels
+    if q.ndim != 4 or k.ndim != 4 or v.ndim != 4:
+        raise ValueError("q, k, and v must all have shape (batch, heads, sequence, dimension)")
+    if tuple(q.shape) != tuple(k.shape) or tuple(q.shape) != tuple(v.shape):
+        raise ValueError(f"q, k, and v shapes must match, got {tuple(q.shape)}, {tuple(k.shape)}, and {tuple(v.shape)}")
+    if not _sink_ok(sink_omega):
+        raise ValueError("sink_omega must be finite and nonnegative")
+    if block_q <= 0 or block_k <= 0:
+        raise ValueError("block_q and block_k must be positive")
+    _, _, seq_len, head_dim = q.shape
+    if head_dim <= 0:
+        raise ValueError("head dimension must be positive")
+    if head_dim > 128 and head_dim % 128 != 0:
+        raise ValueError("head dimensions above 128 must be divisible by 128 for TPU layout")
+    if seq_len % block_q != 0 or seq_len % block_k != 0:
+        raise ValueError(f"seq_len ({seq_len}) must be divisible by block_q ({block_q}) and block_k ({block_k})")
+    if valid_seq_len is not None and not 0 < valid_seq_len <= seq_len:
+        raise ValueError("valid_seq_len must be in [1, seq_len]")
+    host_checks_float(q, k, v)
+    return _launch_fwd(q, k, v, sink_omega, causal, valid_seq_len, return_denominator)
+
+
+def tiled_afa_forward(q, k, v, sink_omega: float = 0.5, causal: bool = False, block_q: int = 128,
+                      block_k: int = 128, valid_seq_len: Optional[int] = None, return_denominator: bool = False):
+    """The reference's XLA-tiled forward (src/kernels/pallas_afa.py:330-406).
+
+    Same math as ``pallas_afa_forward``; argument checks and messages follow
+    pallas_afa.py:342-353.
+    """
+    if q.ndim != 4 or tuple(q.shape) != tuple(k.shape) or tuple(q.shape) != tuple(v.shape):
+        raise ValueError("q, k, and v must have the same four-dimensional shape")
+    if not _sink_ok(sink_omega):
+        raise ValueError("sink_omega must be finite and nonnegative")
+    if block_q <= 0 or block_k <= 0:
+        raise ValueError("block_q and block_k must be positive")
+    seq_len = q.shape[2]
+    if seq_len % block_q != 0 or seq_len % block_k != 0:
+        raise ValueError("sequence length must be divisible by both tile dimensions")
+    if valid_seq_len is not None and not 0 < valid_seq_len <= seq_len:
+        raise ValueError("valid_seq_len must be in [1, seq_len]")
+    host_checks_float(q, k, v)
+    return _launch_fwd(q, k, v, sink_omega, causal, valid_seq_len, return_denominator)
+
+
+def pallas_afa(q, k, v, sink_omega: float = 0.5, causal: bool = False, block_q: int = 128, block_k: int = 128,
+               valid_seq_len: Optional[int] = None):
+    """Forward of the reference's custom-VJP entry (src/kernels/pallas_afa.py:579-612).
+
+    The analytical backward (pallas_afa.py:409-522) is not part of this build;
+    the returned tensor carries no autograd graph.
+    """
+    return pallas_afa_forward(q, k, v, sink_omega=sink_omega, causal=causal, block_q=block_q, block_k=block_k,
+                              valid_seq_len=valid_seq_len)
+
+
+def algebraic_flash_attention(q, k, v, sink_omega: float = 0.5, causal: bool = False, block_q: int = 128,
+                              block_k: int = 128):
+    """Unified entry for any sequence length (src/kernels/pallas_afa.py:695-739).
+
+    The reference pads L up to lcm(block_q, block_k) with zero rows and masks
+    the padded keys through ``valid_seq_len``; the padded query rows are sliced
+    off. The B200 kernels mask keys at index >= L and skip stores of rows >= L
+    directly, which gives the same result with no padding copies.
+    """
+    if q.ndim != 4 or tuple(q.shape) != tuple(k.shape) or tuple(q.shape) != tuple(v.shape):
+        raise ValueError("q, k, and v must have the same four-dimensional shape")
+    if block_q <= 0 or block_k <= 0:
+        raise ValueError("block_q and block_k must be positive")
+    if not _sink_ok(sink_omega):
+        raise ValueError("sink_omega must be finite and nonnegative")
+    host_checks_float(q, k, v)
+    del block_q, block_k
+    return _launch_fwd(q, k, v, sink_omega, causal, None, False)
+
+
+def afa_decode(q, k_cache, v_cache, sink_omega: float = 0.5, kv_len=None, return_denominator: bool = False,
+               workspace: Optional[torch.Tensor] = None):
+    """One decode step: exact AFA for a single query token over a KV cache.
+
+    q: (B, H, D) or (B, H, 1, D); k_cache, v_cache: (B, H, Lkv, D). ``kv_len``
+    is an int (visible prefix for every batch row) or a per-batch int tensor.
+    Math = ``pallas_afa_forward`` with one query row, non-causal; oracle =
+    reference_afa with Lq = 1 (tests/reference_attention.py:44-59).
+    """
+    if not _sink_ok(sink_omega):
+        raise ValueError("sink_omega must be finite and nonnegative")
+    if k_cache.ndim != 4 or tuple(k_cache.shape) != tuple(v_cache.shape):
+        raise ValueError("k_cache and v_cache must have the same (batch, heads, length, dim) shape")
+    squeeze = q.ndim == 3
+    b, h, lkv, d = k_cache.shape
+    if tuple(q.shape) not in ((b, h, d), (b, h, 1, d)):
+        raise ValueError(f"q must have shape (B, H, D) or (B, H, 1, D) matching the cache, got {tuple(q.shape)}")
+    host_checks_float(q, k_cache, v_cache)
+    lens_t = None
+    scalar_len = 0
+    if kv_len is not None:
+        if isinstance(kv_len, int):
+            if not 0 < kv_len <= lkv:
+                raise ValueError("kv_len must be in [1, cache length]")
+            scalar_len = kv_len
+        else:
+            lens_t = torch.as_tensor(kv_len, dtype=torch.int32)
+    st = Staged(q, k_cache, v_cache)
+    qt, kt, vt = st.tensors
+    if lens_t is not None:
+        lens_t = lens_t.to(st.device).contiguous()
+        if lens_t.numel() != b:
+            raise ValueError("kv_len must have one entry per batch row")
+    code = _lib.dtype_code(qt.dtype)
+    out = torch.empty((b, h, d), dtype=qt.dtype, device=qt.device)
+    den = torch.empty((b, h), dtype=_lib.accum_dtype(qt.dtype), device=qt.device)
+    lib = _lib.load()
+    need = lib.afa_decode_workspace_bytes(b, h, lkv, d)
+    if need:
+        if workspace is None or workspace.numel() * workspace.element_size() < need:
+            workspace = torch.empty(need, dtype=torch.uint8, device=qt.device)
+        ws_ptr, ws_bytes = workspace.data_ptr(), workspace.numel() * workspace.element_size()
+    else:
+        ws_ptr, ws_bytes = None, 0
+    with torch.cuda.device(qt.device):
+        rc = lib.afa_decode(qt.data_ptr(), kt.data_ptr(), vt.data_ptr(), out.data_ptr(), den.data_ptr(), b, h, lkv, d,
+                            code, float(sink_omega), lens_t.data_ptr() if lens_t is not None else None, scalar_len,
+                            ws_ptr, ws_bytes, _lib.stream_ptr(qt.device))
+    _lib.check(rc, "afa_decode")
+    if not squeeze:
+        out = out.unsqueeze(2)
+        den = den.unsqueeze(2)
+    if return_denominator:
+        return st.back(out), st.back(den.unsqueeze(-1))
+    return st.back(out)
+
+
+def decode_workspace_bytes(batch: int, heads: int, kv_capacity: int, head_dim: int) -> int:
+    """Scratch bytes ``afa_decode`` needs for this shape (0 when it needs none)."""
+    return int(_lib.load().afa_decode_workspace_bytes(batch, heads, kv_capacity, head_dim))
+
+
+def hop_forward(q, k, v, problems, causal, mode, o_acc=None, d_acc=None, out=None, d_total=None,
+                sink_omega: float = 0.5) -> None:
+    """Grouped partial forward over up to four (query segment, key segments)
+    problems -- one ring hop (src/kernels/pallas_afa.py:634-654). All tensors are
+    CUDA tensors; ``problems`` is a list of
+    ``(q_row0, q_len, q_pos0, [(k_row0, k_len, k_pos0), ...])``.
+    """
+    flat = []
+    for qr, ql, qp, segs in problems:
+        if not 1 <= len(segs) <= 2:
+            raise ValueError("each problem needs one or two key segments")
+        row = [qr, ql, qp, len(segs)]
+        for s in segs:
+            row += list(s)
+        if len(segs) == 1:
+            row += [0, 0, 0]
+        flat += row
+    arr = (ctypes.c_int * len(flat))(*flat)
+    b, h, lq, d = q.shape
+    lk = k.shape[2]
+    lib = _lib.load()
+    ptr = lambda t: None if t is None else t.data_ptr()  # noqa: E731
+    with torch.cuda.device(q.device):
+        rc = lib.afa_fwd_hop(q.data_ptr(), k.data_ptr(), v.data_ptr(), ptr(o_acc), ptr(d_acc), ptr(out), ptr(d_total),
+                             b, h, lq, lk, d, _lib.dtype_code(q.dtype), arr, len(problems), int(bool(causal)),
+                             int(mode), float(sink_omega), _lib.stream_ptr(q.device))
+    _lib.check(rc, "afa_fwd_hop")
+
+
+def scale_for(head_dim: int) -> float:
+    """Score scale of the reference, float(1/sqrt(D)) (pallas_afa.py:190)."""
+    return float(1.0 / math.sqrt(head_dim))

@@ -1,0 +1,64 @@
+"""algebraic_softmax and octic_kernel on B200, behind the reference's signatures.
+
+* ``algebraic_softmax(scores, sink_omega=0.5, eps=1e-5)`` -- src/attention.py:88-91
+  (forward of _attention_forward, :59-67): AVN over the last axis, then
+  rho^8 / (sum rho^8 + sink). fp32 accumulation for half inputs, fp64 kept,
+  output in the input dtype. ValueError / TypeError conditions follow
+  attention.py:60-63 and primitives.py:17-21, 56-61.
+* ``octic_kernel(x)`` -- src/attention.py:47-50: rho(x)^8 elementwise.
+"""
+from __future__ import annotations
+
+import numpy as np
+import torch
+
+from . import _lib
+from ._tensors import Staged, host_checks_float
+
+__all__ = ["algebraic_softmax", "octic_kernel"]
+
+
+def _as_array(x):
+    if isinstance(x, (torch.Tensor, np.ndarray)):
+        return x
+    return np.asarray(x)
+
+
+def algebraic_softmax(scores, sink_omega: float = 0.5, eps: float = 1e-5):
+    """AVN-bounded octic attention weights over the last axis (src/attention.py:88-91)."""
+    if not 0 <= sink_omega < float("inf"):
+        raise ValueError("sink_omega must be finite and nonnegative")
+    if not 0 < eps < float("inf"):
+        raise ValueError("eps must be finite and positive")
+    scores = _as_array(scores)
+    host_checks_float(scores)
+    if scores.ndim == 0 or scores.shape[-1] == 0:
+        raise ValueError("AVN needs a nonempty feature axis")
+    st = Staged(scores)
+    (x,) = st.tensors
+    y = torch.empty_like(x)
+    cols = x.shape[-1]
+    rows = x.numel() // cols
+    with torch.cuda.device(x.device):
+        rc = _lib.load().algebraic_softmax_fwd(x.data_ptr(), y.data_ptr(), rows, cols, _lib.dtype_code(x.dtype),
+                                               float(sink_omega), float(eps), _lib.stream_ptr(x.device))
+    _lib.check(rc, "algebraic_softmax")
+    return st.back(y)
+
+
+def octic_kernel(x):
+    """rho(x)^8 via three squarings after evaluating rho (src/attention.py:47-50).
+
+    Evaluated in the accumulation dtype with the reference's cancellation-free
+    branch for negative x (attention.py:18-26), returned in x's dtype.
+    """
+    x = _as_array(x)
+    host_checks_float(x)
+    st = Staged(x)
+    (xt,) = st.tensors
+    y = torch.empty_like(xt)
+    with torch.cuda.device(xt.device):
+        rc = _lib.load().afa_octic(xt.data_ptr(), y.data_ptr(), xt.numel(), _lib.dtype_code(xt.dtype),
+                                   _lib.stream_ptr(xt.device))
+    _lib.check(rc, "octic_kernel")
+    return st.back(y)

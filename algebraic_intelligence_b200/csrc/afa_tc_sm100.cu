@@ -1,0 +1,474 @@
+// AFA prefill forward on the B200 5th-generation tensor cores (tcgen05 + TMEM).
+//
+// Reference: afa_kernel / pallas_afa_forward (src/kernels/pallas_afa.py:52-151,
+// :154-264). Per (batch, head, 128-row query tile) the reference accumulates
+//     S = (Q K^T) * scale                (fp32 accumulation, :104-110)
+//     P = rho(S)^8, masked               (:113-124)
+//     O += P.astype(v.dtype) V           (fp32 accumulation, :132-137)
+//     d += rowsum(P)                     (fp32 P, :139)
+// and finishes with O / (d + sink) and d_total = d + sink (:142-151). There is
+// no running maximum, so tiles add up with no rescaling.
+//
+// B200 design (one CTA per SM, 384 threads, two 128-row query tiles per CTA):
+//   warp 0      TMA producer: Q once, then K_j / V_j tiles through a ring of
+//               shared-memory slots (128-byte swizzle, no multicast).
+//   warp 1      allocates 512 TMEM columns and issues every tcgen05.mma from one
+//               thread: S_i = Q_i K_j^T (A, B from shared memory) and
+//               O_i += P_i V_j (A = P from TMEM, B = V from shared memory).
+//   warps 4-7   "softmax" group of query tile 0, warps 8-11 of tile 1: each
+//               thread owns one query row (one TMEM lane), reads its S row,
+//               applies the octic map and masks in registers, keeps the fp32
+//               row sum, and writes P as packed bf16 back over the first 64
+//               columns of its S tile. The two groups alternate with the tensor
+//               core (while group 0 maps S_0, the MMA pipe runs tile 1).
+//   epilogue    the same groups read O from TMEM, divide once by (d + sink) and
+//               store bf16 rows (or add the raw numerator / row sum into fp32
+//               accumulators for ring hops).
+// TMEM columns: S0/P0 [0,128), S1/P1 [128,256), O0 [256,256+D), O1 [256+D, ...).
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include "afa_common.cuh"
+#include "afa_internal.h"
+
+namespace afa {
+namespace {
+
+template <int HD>
+struct TcCfg {
+  static constexpr int kThreads = 384;
+  static constexpr int BM = 128;
+  static constexpr int BN = 128;
+  static constexpr int KSUB = HD / 64;             // 64-element (128 B) column blocks
+  static constexpr int SUB_BYTES = 128 * 128;      // 128 rows x 128 B
+  static constexpr int TILE_BYTES = KSUB * SUB_BYTES;
+  static constexpr int NSLOT = (HD == 128) ? 4 : 8;
+  static constexpr int Q_OFF = 0;
+  static constexpr int KV_OFF = 2 * TILE_BYTES;
+  static constexpr int BAR_OFF = KV_OFF + NSLOT * TILE_BYTES;
+  static constexpr int NBAR = 1 + 2 * NSLOT + 2 + 2 + 2 + 1;
+  static constexpr int SMEM_BYTES = BAR_OFF + NBAR * 8 + 16 + 1024;
+  static constexpr uint32_t TMEM_COLS = 512;
+  __device__ static constexpr uint32_t s_col(int i) { return static_cast<uint32_t>(i) * 128u; }
+  __device__ static constexpr uint32_t o_col(int i) { return 256u + static_cast<uint32_t>(i) * HD; }
+};
+
+// Key tiles of one segment visible from a query tile whose last valid row sits
+// at global position qpos_last.
+__device__ __forceinline__ int seg_tiles(const Segment& ks, int causal, int qpos_last) {
+  int n = ks.len;
+  if (causal) {
+    const int m = qpos_last - ks.pos0 + 1;
+    n = m < n ? m : n;
+  }
+  return n <= 0 ? 0 : (n + 127) / 128;
+}
+
+struct KvTile {
+  int row;  // first row of the tile in the per-(b,h) K/V tensor
+  int pos;  // global position of that row
+  int lim;  // valid keys in the tile (1..128)
+};
+
+__device__ __forceinline__ KvTile kv_tile(const Problem& P, int cnt_seg0, int t) {
+  const int s = (t < cnt_seg0) ? 0 : 1;
+  const int jj = s ? t - cnt_seg0 : t;
+  const Segment& ks = P.k[s];
+  KvTile kt;
+  kt.row = ks.row0 + jj * 128;
+  kt.pos = ks.pos0 + jj * 128;
+  const int lim = ks.len - jj * 128;
+  kt.lim = lim < 128 ? lim : 128;
+  return kt;
+}
+
+// Octic map of one 32-column chunk of a score row, written back as 16 packed
+// bf16 pairs. MASK selects the per-element visibility test.
+template <bool MASK>
+__device__ __forceinline__ float map_chunk(const uint32_t (&sv)[32], uint32_t (&pk)[16], float scale, int key0,
+                                           int lim, int causal, int kpos0, int qpos) {
+  float a0 = 0.f, a1 = 0.f;
+#pragma unroll
+  for (int e = 0; e < 32; e += 2) {
+    float p0 = octic_fast(__uint_as_float(sv[e]) * scale);
+    float p1 = octic_fast(__uint_as_float(sv[e + 1]) * scale);
+    if (MASK) {
+      const int c0 = key0 + e, c1 = c0 + 1;
+      const bool v0 = (c0 < lim) && (!causal || kpos0 + c0 <= qpos);
+      const bool v1 = (c1 < lim) && (!causal || kpos0 + c1 <= qpos);
+      p0 = v0 ? p0 : 0.f;
+      p1 = v1 ? p1 : 0.f;
+    }
+    a0 += p0;
+    a1 += p1;
+    pk[e >> 1] = pack_bf16x2(p0, p1);
+  }
+  return a0 + a1;
+}
+
+template <int HD>
+__global__ void __launch_bounds__(384, 1)
+    afa_tc_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                      const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ Launch L) {
+  using C = TcCfg<HD>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::BAR_OFF);
+  uint64_t* q_full = bars;
+  uint64_t* kv_full = bars + 1;
+  uint64_t* kv_empty = kv_full + C::NSLOT;
+  uint64_t* s_full = kv_empty + C::NSLOT;
+  uint64_t* p_full = s_full + 2;
+  uint64_t* o_full = p_full + 2;
+  uint64_t* drain = o_full + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int bh = blockIdx.x;
+  // Heaviest work first: the problem axis is walked backwards, so the last
+  // (most causal keys) query tiles of every head start in the first wave.
+  const int cta = gridDim.y - 1 - blockIdx.y;
+  int pi = 0;
+#pragma unroll
+  for (int i = 1; i < kMaxProblems; ++i)
+    if (i < L.nprob && cta >= L.prob[i].cta0) pi = i;
+  const Problem& P = L.prob[pi];
+  const int r0 = (cta - P.cta0) * 256;  // first row of query tile 0 in the q segment
+
+  // Key tiles per query tile. Only the last key segment may be partially
+  // visible, which makes tile 0's tiles a prefix of tile 1's.
+  const bool q1_live = r0 + 128 < P.q.len;
+  const int last0 = min(r0 + 127, P.q.len - 1);
+  const int last1 = q1_live ? min(r0 + 255, P.q.len - 1) : last0;
+  int cnt0[2] = {0, 0}, cnt1[2] = {0, 0};
+#pragma unroll
+  for (int s = 0; s < kMaxKSegs; ++s) {
+    if (s < P.nk) {
+      cnt0[s] = seg_tiles(P.k[s], L.causal, P.q.pos0 + last0);
+      cnt1[s] = seg_tiles(P.k[s], L.causal, P.q.pos0 + last1);
+    }
+  }
+  const int n1 = cnt1[0] + cnt1[1];
+  const int n0 = (P.nk == 1 || cnt0[0] == cnt1[0]) ? cnt0[0] + cnt0[1] : n1;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int s = 0; s < C::NSLOT; ++s) {
+      mbar_init(kv_full + s, 1);
+      mbar_init(kv_empty + s, 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(s_full + i, 1);
+      mbar_init(p_full + i, 128);
+      mbar_init(o_full + i, 1);
+    }
+    mbar_init(drain, 1);
+    fence_barrier_init();
+    fence_proxy_async_smem();
+    prefetch_tmap(&tm_q);
+    prefetch_tmap(&tm_k);
+    prefetch_tmap(&tm_v);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, C::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------------ TMA
+    if (lane == 0 && n1 > 0) {
+      mbar_arrive_expect_tx(q_full, 2 * C::TILE_BYTES);
+      for (int i = 0; i < 2; ++i)
+        for (int h = 0; h < C::KSUB; ++h)
+          tma_load_3d(smem + C::Q_OFF + (i * C::KSUB + h) * C::SUB_BYTES, &tm_q, q_full, 64 * h,
+                      P.q.row0 + r0 + 128 * i, bh);
+      int issued = 0;
+      for (int t = 0; t < n1; ++t) {
+        const KvTile kt = kv_tile(P, cnt1[0], t);
+        bool ok = true;
+        for (int kv = 0; kv < 2; ++kv) {
+          const int u = 2 * t + kv;
+          const int slot = u % C::NSLOT;
+          if (!mbar_wait(kv_empty + slot, ((u / C::NSLOT) & 1) ^ 1, L.status, kDevTimeoutProducer)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(kv_full + slot, C::TILE_BYTES);
+          for (int h = 0; h < C::KSUB; ++h)
+            tma_load_3d(smem + C::KV_OFF + (slot * C::KSUB + h) * C::SUB_BYTES, kv ? &tm_v : &tm_k,
+                        kv_full + slot, 64 * h, kt.row, bh);
+          issued = u + 1;
+        }
+        if (!ok) break;
+      }
+      // Do not leave the CTA while loads into its shared memory are in flight.
+      (void)mbar_wait(q_full, 0, nullptr, 0);
+      for (int u = issued - C::NSLOT < 0 ? 0 : issued - C::NSLOT; u < issued; ++u)
+        (void)mbar_wait(kv_full + (u % C::NSLOT), (u / C::NSLOT) & 1, nullptr, 0);
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------------ MMA
+    if (lane == 0 && n1 > 0) {
+      constexpr uint32_t idesc_s = idesc_bf16_f32(128, 128, false);
+      constexpr uint32_t idesc_o = idesc_bf16_f32(128, HD, true);
+      const uint32_t q_base = smem_u32(smem + C::Q_OFF);
+      const uint32_t kv_base = smem_u32(smem + C::KV_OFF);
+      auto issue_s = [&](int i, int slot) {
+#pragma unroll
+        for (int kk = 0; kk < HD / 16; ++kk) {
+          const uint32_t off = (kk & 3) * 32;
+          const uint64_t a = sw128_desc(q_base + (i * C::KSUB + (kk >> 2)) * C::SUB_BYTES + off, 16, 1024);
+          const uint64_t b = sw128_desc(kv_base + (slot * C::KSUB + (kk >> 2)) * C::SUB_BYTES + off, 16, 1024);
+          umma_ss(tmem + C::s_col(i), a, b, idesc_s, kk > 0 ? 1u : 0u);
+        }
+      };
+      auto issue_o = [&](int i, int slot, bool acc) {
+#pragma unroll
+        for (int kk = 0; kk < C::BN / 16; ++kk) {
+          const uint64_t b = sw128_desc(kv_base + slot * C::TILE_BYTES + kk * 2048, C::SUB_BYTES, 1024);
+          umma_ts(tmem + C::o_col(i), tmem + C::s_col(i) + kk * 8, b, idesc_o, (acc || kk > 0) ? 1u : 0u);
+        }
+      };
+      bool ok = mbar_wait(q_full, 0, L.status, kDevTimeoutMma) && mbar_wait(kv_full + 0, 0, L.status, kDevTimeoutMma);
+      if (ok) {
+        tc_fence_after();
+        if (n0 > 0) {
+          issue_s(0, 0);
+          umma_commit(s_full + 0);
+        }
+        issue_s(1, 0);
+        umma_commit(s_full + 1);
+        umma_commit(kv_empty + 0);
+      }
+      for (int t = 0; ok && t < n1; ++t) {
+        const int uv = 2 * t + 1, sv = uv % C::NSLOT;
+        if (!(ok = mbar_wait(kv_full + sv, (uv / C::NSLOT) & 1, L.status, kDevTimeoutMma))) break;
+        tc_fence_after();
+        if (t < n0) {
+          if (!(ok = mbar_wait(p_full + 0, t & 1, L.status, kDevTimeoutMma))) break;
+          tc_fence_after();
+          issue_o(0, sv, t > 0);
+          if (t + 1 == n0) umma_commit(o_full + 0);
+        }
+        const bool more = t + 1 < n1;
+        const int uk = 2 * t + 2, sk = uk % C::NSLOT;
+        if (more) {
+          if (!(ok = mbar_wait(kv_full + sk, (uk / C::NSLOT) & 1, L.status, kDevTimeoutMma))) break;
+          tc_fence_after();
+          if (t + 1 < n0) {
+            issue_s(0, sk);
+            umma_commit(s_full + 0);
+          }
+        }
+        if (!(ok = mbar_wait(p_full + 1, t & 1, L.status, kDevTimeoutMma))) break;
+        tc_fence_after();
+        issue_o(1, sv, t > 0);
+        umma_commit(kv_empty + sv);
+        if (t + 1 == n1) umma_commit(o_full + 1);
+        if (more) {
+          issue_s(1, sk);
+          umma_commit(s_full + 1);
+          umma_commit(kv_empty + sk);
+        }
+      }
+      // Every MMA this thread issued must finish before TMEM is released.
+      umma_commit(drain);
+      (void)mbar_wait(drain, 0, nullptr, 0);
+    }
+  } else if (warp >= 4) {
+    // --------------------------------------------------- octic map + epilogue
+    const int wg = (warp - 4) >> 2;
+    const int sub = warp & 3;
+    const int row = sub * 32 + lane;
+    const int rloc = r0 + 128 * wg + row;
+    const int qpos = P.q.pos0 + rloc;
+    const int qfirst = P.q.pos0 + r0 + 128 * wg;
+    const uint32_t lane_off = static_cast<uint32_t>(sub * 32) << 16;
+    const uint32_t s_tm = tmem + C::s_col(wg) + lane_off;
+    const uint32_t o_tm = tmem + C::o_col(wg) + lane_off;
+    const int n = wg ? n1 : n0;
+    const float scale = L.scale;
+    float dsum = 0.f;
+    bool ok = true;
+    for (int t = 0; t < n; ++t) {
+      ok = mbar_wait(s_full + wg, t & 1, L.status, kDevTimeoutSoftmax);
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok) break;
+      tc_fence_after();
+      const KvTile kt = kv_tile(P, cnt1[0], t);
+      const bool need_mask = kt.lim < 128 || (L.causal && kt.pos + 127 > qfirst);
+      float part = 0.f;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint32_t sv[32];
+        uint32_t pk[16];
+        tmem_ld32(s_tm + 32 * c, sv);
+        tmem_ld_wait();
+        if (need_mask)
+          part += map_chunk<true>(sv, pk, scale, 32 * c, kt.lim, L.causal, kt.pos, qpos);
+        else
+          part += map_chunk<false>(sv, pk, scale, 32 * c, kt.lim, L.causal, kt.pos, qpos);
+        tmem_st16(s_tm + 16 * c, pk);
+      }
+      tmem_st_wait();
+      tc_fence_before();
+      mbar_arrive(p_full + wg);
+      dsum += part;
+    }
+    bool have_o = false;
+    if (ok && n > 0) {
+      ok = mbar_wait(o_full + wg, 0, L.status, kDevTimeoutEpilogue);
+      ok = __all_sync(0xffffffffu, ok);
+      if (ok) {
+        tc_fence_after();
+        have_o = true;
+      }
+    }
+    const bool row_ok = rloc < P.q.len;
+    const long long grow = static_cast<long long>(bh) * L.lq + P.q.row0 + rloc;
+    const bool fin = L.mode == kFinal || L.mode == kAccumFinal;
+    const bool add_prev = L.mode == kAccumRaw || L.mode == kAccumFinal;
+    float* acc_row = fin && !add_prev ? nullptr : static_cast<float*>(L.o_acc) + grow * HD;
+    const float dprev = (row_ok && add_prev) ? static_cast<const float*>(L.d_acc)[grow] : 0.f;
+    const float drow = dsum + dprev;
+    const float denom = drow + L.sink;
+    const float inv = 1.0f / denom;
+    __nv_bfloat16* orow = static_cast<__nv_bfloat16*>(L.out) + grow * HD;
+#pragma unroll
+    for (int c = 0; c < HD / 32; ++c) {
+      uint32_t ov[32];
+      __syncwarp();  // tcgen05.ld is warp-collective; rows that skipped the store rejoin here
+      if (have_o) {
+        tmem_ld32(o_tm + 32 * c, ov);
+        tmem_ld_wait();
+      } else {
+#pragma unroll
+        for (int e = 0; e < 32; ++e) ov[e] = 0u;
+      }
+      if (!row_ok) continue;
+      float x[32];
+#pragma unroll
+      for (int e = 0; e < 32; ++e) x[e] = __uint_as_float(ov[e]);
+      if (add_prev) {
+        const float4* src = reinterpret_cast<const float4*>(acc_row + 32 * c);
+#pragma unroll
+        for (int w = 0; w < 8; ++w) {
+          const float4 y = src[w];
+          x[4 * w + 0] += y.x;
+          x[4 * w + 1] += y.y;
+          x[4 * w + 2] += y.z;
+          x[4 * w + 3] += y.w;
+        }
+      }
+      if (fin) {
+        uint4* dst = reinterpret_cast<uint4*>(orow + 32 * c);
+#pragma unroll
+        for (int w = 0; w < 4; ++w) {
+          uint4 pkt;
+          pkt.x = pack_bf16x2(x[8 * w + 0] * inv, x[8 * w + 1] * inv);
+          pkt.y = pack_bf16x2(x[8 * w + 2] * inv, x[8 * w + 3] * inv);
+          pkt.z = pack_bf16x2(x[8 * w + 4] * inv, x[8 * w + 5] * inv);
+          pkt.w = pack_bf16x2(x[8 * w + 6] * inv, x[8 * w + 7] * inv);
+          dst[w] = pkt;
+        }
+      } else {
+        float4* dst = reinterpret_cast<float4*>(acc_row + 32 * c);
+#pragma unroll
+        for (int w = 0; w < 8; ++w) dst[w] = make_float4(x[4 * w + 0], x[4 * w + 1], x[4 * w + 2], x[4 * w + 3]);
+      }
+    }
+    if (row_ok) {
+      if (fin) {
+        if (L.dtot) static_cast<float*>(L.dtot)[grow] = denom;
+      } else {
+        static_cast<float*>(L.d_acc)[grow] = drow;
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem, C::TMEM_COLS);
+  }
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static bool tried = false;
+  if (!tried) {
+    tried = true;
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }
+  return fn;
+}
+
+// 3-D view (d, rows, batch*heads) of a contiguous (B, H, rows, d) bf16 tensor;
+// box = 64 columns (128 B, the swizzle span) x 128 rows x 1.
+bool make_tmap(CUtensorMap* m, const void* base, int d, int rows, int bh) {
+  auto fn = encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[3] = {static_cast<cuuint64_t>(d), static_cast<cuuint64_t>(rows), static_cast<cuuint64_t>(bh)};
+  cuuint64_t strides[2] = {static_cast<cuuint64_t>(d) * 2, static_cast<cuuint64_t>(d) * 2 * rows};
+  cuuint32_t box[3] = {64, 128, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+template <int HD>
+cudaError_t launch_hd(const Launch& L, cudaStream_t stream, const char** detail) {
+  using C = TcCfg<HD>;
+  static bool attr_set[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 64 && !attr_set[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(afa_tc_fwd_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         C::SMEM_BYTES);
+    if (e != cudaSuccess) {
+      *detail = "cudaFuncSetAttribute(max dynamic shared memory) failed";
+      return e;
+    }
+    attr_set[dev] = true;
+  }
+  CUtensorMap tq, tk, tv;
+  const int bh = L.B * L.H;
+  if (!make_tmap(&tq, L.q, HD, L.lq, bh) || !make_tmap(&tk, L.k, HD, L.lk, bh) ||
+      !make_tmap(&tv, L.v, HD, L.lk, bh)) {
+    *detail = "cuTensorMapEncodeTiled failed (pointer must be 16-byte aligned)";
+    return cudaErrorInvalidValue;
+  }
+  Launch LL = L;
+  const int total = assign_ctas(LL, 256);
+  if (total == 0) return cudaSuccess;
+  dim3 grid(bh, total);
+  afa_tc_fwd_kernel<HD><<<grid, C::kThreads, C::SMEM_BYTES, stream>>>(tq, tk, tv, LL);
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+bool tc_fwd_supported(int dtype, int d) { return dtype == kBF16 && (d == 64 || d == 128); }
+
+cudaError_t launch_tc_fwd(Launch L, int dtype, cudaStream_t stream, const char** detail) {
+  if (!tc_fwd_supported(dtype, L.d)) {
+    *detail = "tensor-core path needs bf16 and head_dim 64 or 128";
+    return cudaErrorInvalidValue;
+  }
+  return L.d == 128 ? launch_hd<128>(L, stream, detail) : launch_hd<64>(L, stream, detail);
+}
+
+}  // namespace afa

@@ -1,0 +1,173 @@
+/*
+ * afa_b200.h -- C ABI of the B200 (sm_100a) Algebraic FlashAttention library
+ * (libafa_b200.so).
+ *
+ * The reference (tasmaikeni13/algebraic-intelligence) is a JAX repository;
+ * its hot path is the Python functions below. Each entry point here is what a
+ * foreign-function binding of that path (ctypes, or an XLA FFI custom-call
+ * handler) calls, with plain pointers and sizes:
+ *
+ *   afa_fwd               <- pallas_afa_forward  (src/kernels/pallas_afa.py:154-264)
+ *                            also the math of tiled_afa_forward (:330-406) and,
+ *                            through valid_len, algebraic_flash_attention (:695-739)
+ *   afa_fwd_hop           <- one hop of distributed_ring_afa (pallas_afa.py:634-654)
+ *   afa_finalize          <- the ring's final divide (pallas_afa.py:661)
+ *   afa_decode            <- no reference counterpart: exact AFA for one query
+ *                            token over a KV cache (pallas_afa_forward with Lq=1)
+ *   algebraic_softmax_fwd <- algebraic_softmax   (src/attention.py:88-91, :59-67)
+ *   afa_octic             <- octic_kernel        (src/attention.py:47-50) and
+ *                            _vmu_octic_kernel   (pallas_afa.py:32-49)
+ *
+ * Conventions
+ *   - Tensors are contiguous, row-major; attention tensors are (B, H, L, D).
+ *   - All buffers are device memory owned by the caller; no entry point
+ *     allocates. Launches are ordered on `stream` (a cudaStream_t; NULL = the
+ *     legacy default stream) and return as soon as the work is queued.
+ *   - dtype codes: AFA_F32, AFA_BF16, AFA_F16, AFA_F64. Accumulators and the
+ *     denominator output (d_total) are float32, or float64 for AFA_F64 inputs.
+ *   - Every entry point returns AFA_OK or an error code and never aborts; the
+ *     message of the last failure on the calling thread is afa_last_error().
+ *   - Kernels that wait on on-chip barriers give up after a bounded time and
+ *     record a non-zero device status; afa_device_status() reads it.
+ */
+#ifndef AFA_B200_H_
+#define AFA_B200_H_
+
+#include <stddef.h>
+
+#if defined(__GNUC__)
+#define AFA_API __attribute__((visibility("default")))
+#else
+#define AFA_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define AFA_F32 0
+#define AFA_BF16 1
+#define AFA_F16 2
+#define AFA_F64 3
+
+#define AFA_OK 0
+#define AFA_ERR_INVALID 1     /* bad shape, pointer or hyperparameter (ValueError in Python) */
+#define AFA_ERR_DTYPE 2       /* dtype not supported (TypeError in Python) */
+#define AFA_ERR_CUDA 3        /* a CUDA runtime call failed */
+#define AFA_ERR_DEVICE 4      /* a kernel reported a device-side failure (bounded wait ran out) */
+
+/* Library version string. */
+AFA_API const char* afa_version(void);
+
+/* Message of the last error returned on the calling thread ("" if none). */
+AFA_API const char* afa_last_error(void);
+
+/*
+ * AFA forward, pallas_afa_forward (pallas_afa.py:154-264).
+ *   q, k, v     (B, H, L, D) in `dtype` (AFA_F32, AFA_BF16 or AFA_F64).
+ *   out         (B, H, L, D) in `dtype`: rho(QK^T/sqrt(D))^8 V / (rowsum + sink).
+ *   d_total     (B, H, L) accumulation dtype: rowsum + sink; may be NULL
+ *               (return_denominator=False).
+ *   causal      key j visible from query i iff j <= i (pallas_afa.py:121-124).
+ *   valid_len   keys with index >= valid_len are dropped (pallas_afa.py:116-118);
+ *               0 means all L keys. Must be in [0, L].
+ * AFA_BF16 with D in {64, 128} runs on the tcgen05 tensor cores; other cases on
+ * the CUDA cores. AFA_F16 returns AFA_ERR_DTYPE: the reference casts P to the
+ * value dtype (pallas_afa.py:133), and rho^8 exceeds the float16 range for
+ * scores above about 2.4.
+ */
+AFA_API int afa_fwd(const void* q, const void* k, const void* v, void* out, void* d_total, int B, int H, int L, int D,
+            int dtype, float sink_omega, int causal, int valid_len, void* stream);
+
+/*
+ * One ring hop (distributed_ring_afa body, pallas_afa.py:634-654), or any
+ * grouped partial forward over up to 4 problems.
+ *   q           (B, H, Lq, D); k, v (B, H, Lk, D).
+ *   o_acc       (B, H, Lq, D) accumulation dtype; d_acc (B, H, Lq): the running
+ *               unnormalised numerator sum P V and row sum sum P.
+ *   out         (B, H, Lq, D) in `dtype`; d_total (B, H, Lq) accumulation dtype
+ *               (may be NULL) -- written by the FINALIZE and ONLY modes.
+ *   problems    host array of nproblems x 10 ints:
+ *                 q_row0, q_len, q_pos0, nk, k0_row0, k0_len, k0_pos0,
+ *                 k1_row0, k1_len, k1_pos0
+ *               A problem maps query rows [q_row0, q_row0+q_len) (global
+ *               positions from q_pos0) onto nk (1 or 2) key segments of K/V.
+ *               With causal, key position <= query position decides
+ *               visibility (pallas_afa.py:640-646); a segment may be wholly
+ *               invisible (no tiles run, the epilogue still does). Query ranges
+ *               of different problems must not overlap; with two key segments
+ *               and causal, the first must be visible to every query row.
+ *   mode        AFA_HOP_STORE      o_acc = O, d_acc = d          (first hop)
+ *               AFA_HOP_ACCUMULATE o_acc += O, d_acc += d        (middle hops)
+ *               AFA_HOP_FINALIZE   out = (o_acc + O) / (d_acc + d + sink),
+ *                                  d_total = d_acc + d + sink    (last hop,
+ *                                  the divide of pallas_afa.py:661 fused in)
+ *               AFA_HOP_ONLY       out = O / (d + sink)          (single hop)
+ *   Rows outside every problem are not touched.
+ */
+#define AFA_HOP_STORE 0
+#define AFA_HOP_ACCUMULATE 1
+#define AFA_HOP_FINALIZE 2
+#define AFA_HOP_ONLY 3
+AFA_API int afa_fwd_hop(const void* q, const void* k, const void* v, void* o_acc, void* d_acc, void* out,
+                        void* d_total, int B, int H, int Lq, int Lk, int D, int dtype, const int* problems,
+                        int nproblems, int causal, int mode, float sink_omega, void* stream);
+
+/*
+ * Ring epilogue (pallas_afa.py:661): out = o_acc / (d_acc + sink) in `dtype`,
+ * d_total = d_acc + sink (may be NULL). rows = B*H*L.
+ */
+AFA_API int afa_finalize(const void* o_acc, const void* d_acc, void* out, void* d_total, long long rows, int D, int dtype,
+                 float sink_omega, void* stream);
+
+/*
+ * Decode step (no reference counterpart; the math of pallas_afa_forward with a
+ * single query row, non-causal).
+ *   q           (B, H, D) -- one token per (batch, head)
+ *   k_cache, v_cache  (B, H, Lkv, D)
+ *   out         (B, H, D); d_total (B, H) float32, may be NULL.
+ *   kv_lens     optional device int32[B]: visible cache length per batch row;
+ *               NULL uses kv_len for all rows (0 = Lkv).
+ *   workspace   device scratch of afa_decode_workspace_bytes(B, H, Lkv, D)
+ *               bytes (may be NULL when that size is 0).
+ * AFA_BF16 (D in 64/128/256) and AFA_F32 (D in 64/128) use the split-KV
+ * streaming kernel; other supported shapes fall back to the CUDA-core
+ * forward kernel.
+ */
+AFA_API int afa_decode(const void* q, const void* k_cache, const void* v_cache, void* out, void* d_total, int B, int H,
+               int Lkv, int D, int dtype, float sink_omega, const int* kv_lens, int kv_len, void* workspace,
+               size_t workspace_bytes, void* stream);
+AFA_API size_t afa_decode_workspace_bytes(int B, int H, int Lkv, int D);
+
+/*
+ * algebraic_softmax (src/attention.py:88-91): rows x cols, last axis
+ * normalised. dtype AFA_F32, AFA_BF16, AFA_F16 (fp32 accumulation) or AFA_F64.
+ * Errors mirror the reference: sink_omega must be finite and >= 0, eps finite
+ * and > 0 (attention.py:60-63), cols > 0 (primitives.py:58-59).
+ */
+AFA_API int algebraic_softmax_fwd(const void* x, void* y, long long rows, int cols, int dtype, double sink_omega,
+                          double eps, void* stream);
+
+/* octic_kernel (src/attention.py:47-50): y = rho(x)^8 elementwise, n elements. */
+AFA_API int afa_octic(const void* x, void* y, long long n, int dtype, void* stream);
+
+/*
+ * Synchronises `stream`, then reads the calling device's status word (0 = no
+ * kernel reported a failure) into *status; clears it when `clear` is non-zero.
+ */
+AFA_API int afa_device_status(void* stream, int* status, int clear);
+
+/*
+ * Failure-detection self-test (no reference counterpart): launches one thread
+ * that waits on an on-chip barrier nothing ever releases, with a wait budget of
+ * budget_ns (at most 2 s). The wait gives up, records status 0x1ff and the
+ * kernel returns; afa_device_status() then reports 0x1ff. Exercises the same
+ * bounded wait every pipelined kernel uses, without faulting or hanging a GPU.
+ */
+AFA_API int afa_selftest_bounded_wait(long long budget_ns, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* AFA_B200_H_ */

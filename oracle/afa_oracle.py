@@ -1,0 +1,249 @@
+"""CPU oracle for the Algebraic FlashAttention (AFA) hot path.
+
+TEST INFRASTRUCTURE ONLY. This module is the checker, never the thing measured or
+shipped: only ``tests/``, ``__graft_entry__.smoke()`` and the CPU-baseline leg of
+``bench.py`` may import it. The product path (``algebraic_intelligence_b200``)
+never calls it and fails loudly when its CUDA library is missing.
+
+It restates, in float64 NumPy, the reference's own ground truth
+(tasmaikeni13/algebraic-intelligence):
+
+* ``octic``            -- tests/reference_attention.py:5-13 (``kernel``): the
+                          branch form rho = sqrt(1+x^2)+x for x >= 0 and
+                          1/(sqrt(1+x^2)-x) for x < 0, then rho**8.
+* ``normalized``       -- tests/reference_attention.py:16-18.
+* ``attention``        -- tests/reference_attention.py:21-24 (AVN over the last
+                          axis, then the sink-normalised octic weights); this is
+                          the math of ``algebraic_softmax`` (src/attention.py:59-67).
+* ``afa``              -- tests/reference_attention.py:44-59 (``reference_afa``),
+                          the exact float64 AFA forward, causal = top-left
+                          aligned ``tril``.
+* ``afa_blocked``      -- the same math evaluated in query-row blocks with
+                          explicit global positions, so configurations whose
+                          full score matrix would not fit in host memory can be
+                          checked; a key at global position c is visible from a
+                          query at position r iff c <= r (src/kernels/pallas_afa.py:
+                          121-124 and :640-646), keys at local index >=
+                          ``valid_len`` are dropped (pallas_afa.py:116-118).
+* ``ring_simulation``  -- the sequence-sharded ring of
+                          src/kernels/pallas_afa.py:618-662, simulated hop by hop
+                          with additive numerator/denominator merging (the CPU
+                          test of the reference does the same by hand,
+                          tests/test_pallas_afa.py:227-271).
+* ``decode``           -- exact AFA for one query token over a KV cache; the
+                          reference has no decode kernel, so its oracle is
+                          ``afa`` with Lq = 1, non-causal.
+
+Parity is pinned by ``tests/test_oracle.py`` against golden vectors that
+``tests/golden/make_golden.py`` produced by importing the reference's own
+``tests/reference_attention.py``, and against the reference's known answers
+(rho(2)^8 = 51841 + 23184*sqrt(5), the negative-tail values, ...).
+"""
+from __future__ import annotations
+
+import numpy as np
+
+__all__ = [
+    "octic",
+    "normalized",
+    "attention",
+    "afa",
+    "afa_blocked",
+    "afa_with_denominator",
+    "ring_simulation",
+    "zigzag_chunks",
+    "decode",
+    "rel_err",
+]
+
+
+def octic(x):
+    """rho(x)^8 in float64 (tests/reference_attention.py:5-13).
+
+    Only the stable branch of each sign is evaluated, so the negative tail keeps
+    full relative precision (x = -1e4 gives a finite, positive value).
+    """
+    x = np.asarray(x, dtype=np.float64)
+    root = np.sqrt(1.0 + x * x)
+    rho = np.empty_like(x)
+    nonneg = x >= 0
+    rho[nonneg] = root[nonneg] + x[nonneg]
+    rho[~nonneg] = 1.0 / (root[~nonneg] - x[~nonneg])
+    return rho ** 8
+
+
+def normalized(x, sink=0.5):
+    """Octic weights over the last axis with a rational sink (reference_attention.py:16-18)."""
+    k = octic(x)
+    return k / (k.sum(axis=-1, keepdims=True) + sink)
+
+
+def attention(x, sink=0.5, eps=1e-5):
+    """algebraic_softmax ground truth (reference_attention.py:21-24).
+
+    AVN: z = x / sqrt(mean(x^2) + eps) over the last axis, then octic weights
+    divided by (sum + sink).
+    """
+    x = np.asarray(x, dtype=np.float64)
+    z = x / np.sqrt(np.mean(x * x, axis=-1, keepdims=True) + eps)
+    return normalized(z, sink)
+
+
+def afa(q, k, v, sink=0.5, causal=False):
+    """Exact AFA forward (reference_attention.py:44-59).
+
+    o = (rho(QK^T/sqrt(D))^8 [masked]) V / (row_sum + sink).
+    """
+    out, _ = afa_with_denominator(q, k, v, sink=sink, causal=causal)
+    return out
+
+
+def afa_with_denominator(q, k, v, sink=0.5, causal=False):
+    """``afa`` plus the per-row denominator d + sink, shape (..., L, 1).
+
+    The denominator is what ``pallas_afa_forward(return_denominator=True)``
+    returns (src/kernels/pallas_afa.py:148-151, :262-263).
+    """
+    q = np.asarray(q, dtype=np.float64)
+    k = np.asarray(k, dtype=np.float64)
+    v = np.asarray(v, dtype=np.float64)
+    scale = 1.0 / np.sqrt(q.shape[-1])
+    s = np.matmul(q, np.swapaxes(k, -1, -2)) * scale
+    p = octic(s)
+    if causal:
+        lq, lk = s.shape[-2], s.shape[-1]
+        visible = np.tril(np.ones((lq, lk), dtype=bool))
+        p = np.where(visible, p, 0.0)
+    denom = p.sum(axis=-1, keepdims=True) + sink
+    return np.matmul(p, v) / denom, denom
+
+
+def afa_blocked(q, k, v, sink=0.5, causal=False, q_pos0=0, k_pos0=0,
+                valid_len=None, block=512, rows=None, raw=False):
+    """AFA in query-row blocks with global positions (float64).
+
+    q: (..., Lq, D), k/v: (..., Lk, D). Query row i sits at global position
+    ``q_pos0 + i``; key j at ``k_pos0 + j``. Causal visibility is
+    ``key_pos <= query_pos``; keys with local index >= ``valid_len`` are
+    dropped. ``rows`` optionally restricts the evaluation to a subset of query
+    rows (an index array), which the bounded CPU baseline uses.
+
+    Returns (out, denom) with denom = row_sum + sink, or, with ``raw=True``,
+    the unnormalised (numerator, row_sum) pair that a ring hop accumulates.
+    """
+    q = np.asarray(q, dtype=np.float64)
+    k = np.asarray(k, dtype=np.float64)
+    v = np.asarray(v, dtype=np.float64)
+    lq, lk = q.shape[-2], k.shape[-2]
+    scale = 1.0 / np.sqrt(q.shape[-1])
+    limit = lk if valid_len is None else min(int(valid_len), lk)
+    row_ids = np.arange(lq) if rows is None else np.asarray(rows)
+    kt = np.swapaxes(k, -1, -2)
+    key_pos = k_pos0 + np.arange(lk)
+    key_ok = np.arange(lk) < limit
+    num = np.zeros(q.shape[:-2] + (len(row_ids), v.shape[-1]))
+    rsum = np.zeros(q.shape[:-2] + (len(row_ids), 1))
+    for start in range(0, len(row_ids), block):
+        sel = row_ids[start:start + block]
+        s = np.matmul(q[..., sel, :], kt) * scale
+        p = octic(s)
+        visible = np.broadcast_to(key_ok, (len(sel), lk))
+        if causal:
+            visible = visible & (key_pos[None, :] <= (q_pos0 + sel)[:, None])
+        p = np.where(visible, p, 0.0)
+        num[..., start:start + len(sel), :] = np.matmul(p, v)
+        rsum[..., start:start + len(sel), :] = p.sum(axis=-1, keepdims=True)
+    if raw:
+        return num, rsum
+    denom = rsum + sink
+    return num / denom, denom
+
+
+def zigzag_chunks(rank, world):
+    """Chunk ids held by ``rank`` under zigzag sequence sharding.
+
+    The sequence is cut into 2*world equal chunks; rank r keeps chunks r and
+    2*world-1-r, which balances causal work across ranks.
+    """
+    return rank, 2 * world - 1 - rank
+
+
+def ring_simulation(q, k, v, world, sink=0.5, causal=False, zigzag=True):
+    """Hop-by-hop simulation of ring AFA (src/kernels/pallas_afa.py:618-662).
+
+    Each simulated rank keeps its query shard; K/V shards travel around the
+    ring; per hop the rank adds the hop's unnormalised numerator and row sum to
+    its accumulators (pallas_afa.py:648-649) and divides once at the end
+    (pallas_afa.py:661). With ``zigzag`` the shards are zigzag chunk pairs,
+    otherwise contiguous blocks as in the reference. Returns the full output in
+    global row order.
+    """
+    q = np.asarray(q, dtype=np.float64)
+    k = np.asarray(k, dtype=np.float64)
+    v = np.asarray(v, dtype=np.float64)
+    length = q.shape[-2]
+    if zigzag:
+        chunk = length // (2 * world)
+        shards = []
+        for r in range(world):
+            a, b = zigzag_chunks(r, world)
+            shards.append([(a * chunk, chunk), (b * chunk, chunk)])
+    else:
+        shard = length // world
+        shards = [[(r * shard, shard)] for r in range(world)]
+    out = np.zeros_like(q)
+    for r in range(world):
+        q_segs = shards[r]
+        acc = [(np.zeros(q.shape[:-2] + (n, v.shape[-1])), np.zeros(q.shape[:-2] + (n, 1)))
+               for _, n in q_segs]
+        for hop in range(world):
+            src = (r - hop) % world
+            for qi, (qp, qn) in enumerate(q_segs):
+                for kp, kn in shards[src]:
+                    num, rs = afa_blocked(q[..., qp:qp + qn, :], k[..., kp:kp + kn, :],
+                                          v[..., kp:kp + kn, :], causal=causal,
+                                          q_pos0=qp, k_pos0=kp, raw=True)
+                    acc[qi][0][...] += num
+                    acc[qi][1][...] += rs
+        for (qp, qn), (num, rs) in zip(q_segs, acc):
+            out[..., qp:qp + qn, :] = num / (rs + sink)
+    return out
+
+
+def decode(q, k_cache, v_cache, sink=0.5, kv_len=None):
+    """Exact AFA for a single query token per (batch, head) over a KV cache.
+
+    q: (B, H, 1, D) or (B, H, D); caches: (B, H, Lkv, D). ``kv_len`` (int or
+    per-batch sequence) limits the visible cache prefix.
+    """
+    q = np.asarray(q, dtype=np.float64)
+    squeeze = q.ndim == 3
+    if squeeze:
+        q = q[:, :, None, :]
+    k_cache = np.asarray(k_cache, dtype=np.float64)
+    v_cache = np.asarray(v_cache, dtype=np.float64)
+    bsz, lkv = q.shape[0], k_cache.shape[2]
+    if kv_len is None:
+        lens = np.full(bsz, lkv)
+    else:
+        lens = np.broadcast_to(np.asarray(kv_len), (bsz,))
+    outs, dens = [], []
+    for b in range(bsz):
+        n = int(lens[b])
+        o, d = afa_with_denominator(q[b:b + 1], k_cache[b:b + 1, :, :n], v_cache[b:b + 1, :, :n],
+                                    sink=sink, causal=False)
+        outs.append(o)
+        dens.append(d)
+    out = np.concatenate(outs, axis=0)
+    den = np.concatenate(dens, axis=0)
+    if squeeze:
+        out, den = out[:, :, 0, :], den[:, :, 0, :]
+    return out, den
+
+
+def rel_err(actual, expected):
+    """max|actual - expected| / max|expected| -- the reference's parity metric
+    (tests/test_pallas_afa.py:85-87, scripts/run_phase6_tpu.py:120-122)."""
+    a = np.asarray(actual, dtype=np.float64)
+    e = np.asarray(expected, dtype=np.float64)
+    return float(np.max(np.abs(a - e)) / max(float(np.max(np.abs(e))), 1e-300))

@@ -1,0 +1,92 @@
+"""Generate the golden fixtures in this directory from the reference's own oracle.
+
+Run in a container that has the reference checkout (it is not needed afterwards):
+
+    python tests/golden/make_golden.py /path/to/algebraic-intelligence
+
+The script imports ``tests/reference_attention.py`` of the reference (pure NumPy,
+float64) *read-only* from the given checkout and evaluates it on the seeded
+inputs of ``inputs.py``. The reference's own tests seed with JAX PRNG keys,
+which cannot be regenerated without JAX, so NumPy ``default_rng`` seeds are used
+instead. Inputs are not stored; their SHA-256 is, and the tests regenerate them
+and check the digest. Small outputs are stored in float64; the two larger ones
+(config 1 and L=180) in float32, which is ample for the 1e-5 parity bar they
+serve. Nothing at test time reads the reference checkout.
+"""
+from __future__ import annotations
+
+import hashlib
+import importlib.util
+import json
+import sys
+from pathlib import Path
+
+import numpy as np
+
+HERE = Path(__file__).resolve().parent
+sys.path.insert(0, str(HERE))
+import inputs  # noqa: E402
+
+
+def _load_reference_oracle(root: Path):
+    path = root / "tests" / "reference_attention.py"
+    spec = importlib.util.spec_from_file_location("_ref_attention_oracle", path)
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return mod, path
+
+
+def main(root: str) -> None:
+    ref, path = _load_reference_oracle(Path(root))
+    out = {}
+    digests = {}
+
+    x = inputs.octic_grid()
+    digests["octic_grid"] = inputs.digest(x)
+    out["octic_y"] = ref.kernel(x)
+
+    x = inputs.softmax_rows()
+    digests["softmax_rows"] = inputs.digest(x)
+    for sink in (0.0, 0.5, 1.0):
+        out[f"asm_y_sink{sink}"] = ref.attention(x, sink)
+
+    x = inputs.softmax_long_rows()
+    digests["softmax_long_rows"] = inputs.digest(x)
+    out["asm_long_y"] = ref.attention(x, 0.5).astype(np.float32)
+
+    q, k, v = inputs.afa_small()
+    digests["afa_small"] = inputs.digest(q, k, v)
+    out["afa_small_y"] = ref.reference_afa(q, k, v, sink=0.5, causal=False)
+    out["afa_small_y_causal"] = ref.reference_afa(q, k, v, sink=0.5, causal=True)
+
+    q, k, v = inputs.afa_l180()
+    digests["afa_l180"] = inputs.digest(q, k, v)
+    out["afa_l180_y"] = ref.reference_afa(q, k, v, sink=0.5, causal=False).astype(np.float32)
+    out["afa_l180_y_causal"] = ref.reference_afa(q, k, v, sink=0.5, causal=True).astype(np.float32)
+
+    q, k, v = inputs.config1()
+    digests["config1"] = inputs.digest(q, k, v)
+    d = q.shape[-1]
+    s = np.matmul(q.astype(np.float64), np.swapaxes(k.astype(np.float64), -1, -2)) / np.sqrt(d)
+    out["cfg1_softmax_o"] = np.matmul(ref.attention(s, 0.5, 1e-5), v.astype(np.float64)).astype(np.float32)
+    out["cfg1_afa_o"] = ref.reference_afa(q, k, v, sink=0.5, causal=False).astype(np.float32)
+
+    q, k, v = inputs.decode_small()
+    digests["decode_small"] = inputs.digest(q, k, v)
+    out["dec_y"] = ref.reference_afa(q, k, v, sink=0.5, causal=False)
+
+    np.savez_compressed(HERE / "golden.npz", **out)
+    meta = {
+        "generator": "tests/golden/make_golden.py",
+        "reference_file": "tests/reference_attention.py",
+        "reference_file_sha256": hashlib.sha256(path.read_bytes()).hexdigest(),
+        "numpy": np.__version__,
+        "input_sha256": digests,
+        "keys": sorted(out),
+    }
+    (HERE / "golden_meta.json").write_text(json.dumps(meta, indent=1) + "\n")
+    print(f"wrote {len(out)} arrays to {HERE / 'golden.npz'}")
+
+
+if __name__ == "__main__":
+    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")

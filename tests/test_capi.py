@@ -1,0 +1,92 @@
+"""The C-ABI library loads and exports every symbol include/afa_b200.h declares;
+argument checks answer before any CUDA call (no GPU needed)."""
+import ctypes
+import re
+
+import pytest
+
+from algebraic_intelligence_b200 import _lib
+
+HEADER = _lib.LIB_PATH.parents[1] / "include" / "afa_b200.h"
+
+
+def declared_symbols():
+    text = HEADER.read_text()
+    return sorted(set(re.findall(r"AFA_API\s+[\w\s\*]+?\b(\w+)\s*\(", text)))
+
+
+def test_header_declares_the_reference_boundary():
+    names = declared_symbols()
+    for required in ("afa_fwd", "afa_fwd_hop", "afa_finalize", "afa_decode", "algebraic_softmax_fwd",
+                     "afa_octic", "afa_last_error"):
+        assert required in names
+
+
+def test_library_exports_every_declared_symbol():
+    lib = _lib.load()
+    for name in declared_symbols():
+        assert hasattr(lib, name), f"libafa_b200.so does not export {name}"
+    assert set(declared_symbols()) == set(_lib.SIGNATURES), "ctypes signatures and header disagree"
+
+
+def test_version_and_error_string():
+    lib = _lib.load()
+    assert b"sm_100a" in lib.afa_version()
+    assert isinstance(lib.afa_last_error(), bytes)
+
+
+def test_fwd_rejects_float16_before_any_cuda_call():
+    lib = _lib.load()
+    rc = lib.afa_fwd(1, 1, 1, 1, None, 1, 1, 128, 64, _lib.AFA_F16, 0.5, 0, 0, None)
+    assert rc == _lib.AFA_ERR_DTYPE
+    assert b"float16" in lib.afa_last_error()
+
+
+@pytest.mark.parametrize("args,needle", [
+    ((None, 1, 1, 1, None, 1, 1, 128, 64, _lib.AFA_BF16, 0.5, 0, 0, None), b"non-null"),
+    ((1, 1, 1, 1, None, 1, 1, 128, 0, _lib.AFA_BF16, 0.5, 0, 0, None), b"head dimension must be positive"),
+    ((1, 1, 1, 1, None, 1, 1, 128, 64, _lib.AFA_BF16, -1.0, 0, 0, None), b"sink_omega"),
+    ((1, 1, 1, 1, None, 1, 1, 128, 64, _lib.AFA_BF16, float("inf"), 0, 0, None), b"sink_omega"),
+    ((1, 1, 1, 1, None, 1, 1, 128, 64, _lib.AFA_BF16, 0.5, 0, 129, None), b"valid_seq_len"),
+])
+def test_fwd_argument_checks(args, needle):
+    lib = _lib.load()
+    assert lib.afa_fwd(*args) == _lib.AFA_ERR_INVALID
+    assert needle in lib.afa_last_error()
+
+
+def test_softmax_argument_checks():
+    lib = _lib.load()
+    assert lib.algebraic_softmax_fwd(1, 1, 1, 4, _lib.AFA_F32, -1.0, 1e-5, None) == _lib.AFA_ERR_INVALID
+    assert b"sink_omega" in lib.afa_last_error()
+    assert lib.algebraic_softmax_fwd(1, 1, 1, 4, _lib.AFA_F32, 0.5, 0.0, None) == _lib.AFA_ERR_INVALID
+    assert b"eps" in lib.afa_last_error()
+    assert lib.algebraic_softmax_fwd(1, 1, 1, 0, _lib.AFA_F32, 0.5, 1e-5, None) == _lib.AFA_ERR_INVALID
+    assert b"nonempty" in lib.afa_last_error()
+    assert lib.algebraic_softmax_fwd(1, 1, 1, 4, 9, 0.5, 1e-5, None) == _lib.AFA_ERR_DTYPE
+
+
+def test_hop_argument_checks():
+    lib = _lib.load()
+    probs = (ctypes.c_int * 20)(0, 128, 0, 1, 0, 128, 0, 0, 0, 0,
+                                64, 128, 64, 1, 0, 128, 0, 0, 0, 0)
+    rc = lib.afa_fwd_hop(1, 1, 1, 1, 1, None, None, 1, 1, 256, 256, 64, _lib.AFA_BF16, probs, 2, 0,
+                         _lib.AFA_HOP_STORE, 0.5, None)
+    assert rc == _lib.AFA_ERR_INVALID and b"overlapping" in lib.afa_last_error()
+    two = (ctypes.c_int * 10)(0, 128, 0, 2, 0, 128, 0, 128, 64, 128)
+    rc = lib.afa_fwd_hop(1, 1, 1, 1, 1, None, None, 1, 1, 128, 256, 64, _lib.AFA_BF16, two, 1, 1,
+                         _lib.AFA_HOP_STORE, 0.5, None)
+    assert rc == _lib.AFA_ERR_INVALID and b"first key segment" in lib.afa_last_error()
+    rc = lib.afa_fwd_hop(1, 1, 1, None, None, None, None, 1, 1, 128, 128, 64, _lib.AFA_BF16, probs, 1, 0,
+                         _lib.AFA_HOP_ACCUMULATE, 0.5, None)
+    assert rc == _lib.AFA_ERR_INVALID and b"o_acc" in lib.afa_last_error()
+
+
+def test_decode_workspace_query():
+    lib = _lib.load()
+    # batch 64 x 32 heads already fills the GPU: no split, no workspace
+    assert lib.afa_decode_workspace_bytes(64, 32, 8192, 128) == 0
+    # one head over a long cache splits the keys and needs (D+1) floats per split
+    n = lib.afa_decode_workspace_bytes(1, 1, 65536, 128)
+    assert n > 0 and n % (129 * 4) == 0
+    assert lib.afa_decode_workspace_bytes(0, 1, 1, 1) == 0

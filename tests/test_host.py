@@ -1,0 +1,225 @@
+"""Host-side logic without a GPU: argument checks with the reference's exception
+types and messages, and the ring plan (zigzag / contiguous sharding, hop modes,
+K/V rotation over gloo)."""
+import os
+
+import numpy as np
+import pytest
+import torch
+
+import algebraic_intelligence_b200 as afa
+from algebraic_intelligence_b200 import _lib
+from algebraic_intelligence_b200.ring import local_segments, ring_loop, ring_plan, shard_sequence, unshard_sequence
+from oracle import afa_oracle as orc
+
+
+# ---------------------------------------------------------------------------
+# Argument checks (src/kernels/pallas_afa.py:167-186, :342-353, :705-708;
+# src/attention.py:60-63; src/primitives.py:17-21, 56-61)
+# ---------------------------------------------------------------------------
+def _x(shape, dtype=np.float32):
+    return np.ones(shape, dtype=dtype)
+
+
+@pytest.mark.parametrize("kwargs,match", [
+    ({"q": _x((2, 64, 8))}, "must all have shape"),
+    ({"k": _x((1, 1, 64, 16))}, "shapes must match"),
+    ({"sink_omega": -1.0}, "sink_omega"),
+    ({"sink_omega": float("nan")}, "sink_omega"),
+    ({"block_q": 0}, "positive"),
+    ({"q": _x((1, 1, 64, 192)), "k": _x((1, 1, 64, 192)), "v": _x((1, 1, 64, 192))}, "divisible by 128"),
+    ({"block_q": 48}, "divisible by block_q"),
+    ({"valid_seq_len": 0}, "valid_seq_len"),
+    ({"valid_seq_len": 65}, "valid_seq_len"),
+])
+def test_pallas_afa_forward_value_errors(kwargs, match):
+    args = {"q": _x((1, 1, 64, 8)), "k": _x((1, 1, 64, 8)), "v": _x((1, 1, 64, 8)), "block_q": 64, "block_k": 64}
+    args.update(kwargs)
+    with pytest.raises(ValueError, match=match):
+        afa.pallas_afa_forward(**args)
+
+
+def test_tiled_rejects_partial_tiles():
+    # tests/test_pallas_afa.py:201-204
+    x = _x((1, 1, 190, 32))
+    with pytest.raises(ValueError, match="divisible"):
+        afa.tiled_afa_forward(x, x, x, block_q=64, block_k=128)
+
+
+def test_integer_inputs_are_type_errors():
+    x = np.ones((1, 1, 64, 8), dtype=np.int32)
+    with pytest.raises(TypeError):
+        afa.pallas_afa_forward(x, x, x, block_q=64, block_k=64)
+    with pytest.raises(TypeError):
+        afa.algebraic_softmax(np.arange(4))
+
+
+@pytest.mark.parametrize("kwargs", [{"sink_omega": -1.0}, {"sink_omega": float("nan")}, {"eps": 0.0},
+                                    {"eps": -1.0}])
+def test_softmax_invalid_hyperparameters(kwargs):
+    # tests/test_attention.py:66-68
+    with pytest.raises(ValueError):
+        afa.algebraic_softmax(np.ones(4), **kwargs)
+
+
+def test_softmax_invalid_input():
+    # tests/test_attention.py:71-74
+    with pytest.raises(TypeError):
+        afa.algebraic_softmax(np.arange(4))
+    with pytest.raises(ValueError):
+        afa.algebraic_softmax(np.ones(()))
+    with pytest.raises(ValueError):
+        afa.algebraic_softmax(np.ones((2, 0)))
+
+
+def test_unified_entry_value_errors():
+    with pytest.raises(ValueError, match="same four-dimensional shape"):
+        afa.algebraic_flash_attention(_x((1, 1, 64, 8)), _x((1, 1, 63, 8)), _x((1, 1, 64, 8)))
+    with pytest.raises(ValueError, match="positive"):
+        afa.algebraic_flash_attention(_x((1, 1, 64, 8)), _x((1, 1, 64, 8)), _x((1, 1, 64, 8)), block_k=-1)
+
+
+# ---------------------------------------------------------------------------
+# Ring plan
+# ---------------------------------------------------------------------------
+@pytest.mark.parametrize("world", [1, 2, 3, 4, 8])
+@pytest.mark.parametrize("layout", ["contiguous", "zigzag"])
+def test_shard_roundtrip(world, layout):
+    x = torch.arange(2 * 3 * 16 * world * 2, dtype=torch.float32).reshape(2, 3, 16 * world, 2)
+    shards = [shard_sequence(x, r, world, layout) for r in range(world)]
+    assert torch.equal(unshard_sequence(shards, layout), x)
+
+
+def _simulate_ring(q, k, v, world, causal, layout, sink=0.5):
+    """Runs ring_plan + ring_loop for every rank in-process; the hop compute is
+    the oracle (the checker), the rotation a list shift."""
+    seq = q.shape[2]
+    qs = [shard_sequence(q, r, world, layout) for r in range(world)]
+    kvs = [torch.stack([shard_sequence(k, r, world, layout), shard_sequence(v, r, world, layout)])
+           for r in range(world)]
+    outs = []
+    for r in range(world):
+        hops = ring_plan(r, world, seq, causal, layout)
+        s = qs[r].shape[2]
+        o_acc = np.zeros(qs[r].shape)
+        d_acc = np.zeros(qs[r].shape[:3])
+        out = np.full(qs[r].shape, np.nan)
+        class _Req:
+            def wait(self):
+                pass
+
+        def rotate(send, recv):
+            recv.copy_(next(visits_after))
+            return [_Req()]
+
+        visits_after = iter([kvs[(r - h) % world] for h in range(1, world)])
+
+        def compute(hop, kk, vv):
+            assert torch.equal(torch.stack([kk, vv]), kvs[hop.src])
+            for qr, ql, qp, segs in hop.problems:
+                num = np.zeros(qs[r].shape[:2] + (ql, q.shape[3]))
+                rs = np.zeros(qs[r].shape[:2] + (ql, 1))
+                for kr, kl, kp in segs:
+                    n_, r_ = orc.afa_blocked(qs[r][:, :, qr:qr + ql].numpy(), kk[:, :, kr:kr + kl].numpy(),
+                                             vv[:, :, kr:kr + kl].numpy(), causal=causal, q_pos0=qp, k_pos0=kp,
+                                             raw=True)
+                    num += n_
+                    rs += r_
+                sl = slice(qr, qr + ql)
+                if hop.mode == _lib.AFA_HOP_STORE:
+                    o_acc[:, :, sl], d_acc[:, :, sl] = num, rs[..., 0]
+                elif hop.mode == _lib.AFA_HOP_ACCUMULATE:
+                    o_acc[:, :, sl] += num
+                    d_acc[:, :, sl] += rs[..., 0]
+                elif hop.mode == _lib.AFA_HOP_FINALIZE:
+                    out[:, :, sl] = (o_acc[:, :, sl] + num) / (d_acc[:, :, sl] + rs[..., 0] + sink)[..., None]
+                else:
+                    out[:, :, sl] = num / (rs + sink)
+
+        ring_loop(qs[r], kvs[r].clone(), hops, compute, rotate if world > 1 else None)
+        assert s == qs[r].shape[2]
+        outs.append(torch.from_numpy(out))
+    return unshard_sequence(outs, layout).numpy()
+
+
+@pytest.mark.parametrize("world", [1, 2, 3, 4])
+@pytest.mark.parametrize("causal", [False, True])
+@pytest.mark.parametrize("layout", ["contiguous", "zigzag"])
+def test_ring_plan_reproduces_global_afa(world, causal, layout):
+    g = torch.Generator().manual_seed(5)
+    q, k, v = (torch.randn(1, 2, 16 * world, 8, generator=g, dtype=torch.float64) for _ in range(3))
+    ring = _simulate_ring(q, k, v, world, causal, layout)
+    assert np.all(np.isfinite(ring)), "a row was never finalised"
+    assert orc.rel_err(ring, orc.afa(q.numpy(), k.numpy(), v.numpy(), causal=causal)) <= 1e-12
+
+
+def test_zigzag_skips_masked_pairs_and_balances_work():
+    world, seq = 8, 8 * 2 * 1024
+    work = []
+    for r in range(world):
+        tiles = 0
+        for hop in ring_plan(r, world, seq, True, "zigzag"):
+            for qr, ql, qp, segs in hop.problems:
+                for kr, kl, kp in segs:
+                    # visible (query, key) pairs of this problem
+                    qpos = np.arange(qp, qp + ql)
+                    tiles += int(np.clip(qpos[:, None] - kp + 1, 0, kl).sum())
+        work.append(tiles)
+    assert max(work) == min(work), work
+    assert sum(work) == seq * (seq + 1) // 2
+
+
+def test_first_hop_covers_every_query_segment():
+    for world in (2, 4, 8):
+        for r in range(world):
+            for layout in ("contiguous", "zigzag"):
+                for causal in (False, True):
+                    hops = ring_plan(r, world, 64 * world, causal, layout)
+                    covered = {p[0] for p in hops[0].problems}
+                    assert covered == {s[0] for s in local_segments(r, world, 64 * world, layout)}
+                    last = {p[0] for p in hops[-1].problems}
+                    assert last == covered  # every row gets its final divide
+
+
+def _gloo_worker(rank, world, port, results):
+    import torch.distributed as dist
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from algebraic_intelligence_b200.ring import _p2p_rotate
+        kv = torch.full((2, 1, 1, 4, 2), float(rank))
+        seen = [kv.clone()]
+        hops = ring_plan(rank, world, 4 * world, False, "contiguous")
+
+        def compute(hop, kk, vv):
+            seen.append(torch.stack([kk, vv]).clone())
+
+        ring_loop(torch.zeros(1, 1, 4, 2), kv, hops, compute,
+                  lambda s, r: _p2p_rotate(s, r, rank, world, None))
+        results[rank] = [int(t[0, 0, 0, 0, 0]) for t in seen[1:]]
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_ring_rotation_over_gloo(world):
+    """Each rank sees the K/V shards of ranks r, r-1, r-2, ... in hop order
+    (the ppermute direction of pallas_afa.py:632, :651-652)."""
+    import socket
+
+    import torch.multiprocessing as mp
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    ctx = mp.get_context("spawn")
+    mgr = ctx.Manager()
+    results = mgr.dict()
+    procs = [ctx.Process(target=_gloo_worker, args=(r, world, port, results)) for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(120)
+        assert p.exitcode == 0
+    for r in range(world):
+        assert results[r] == [(r - h) % world for h in range(world)]

@@ -1,0 +1,108 @@
+"""Pins the CPU oracle to the reference (no GPU needed).
+
+The oracle (oracle/afa_oracle.py) restates tests/reference_attention.py of the
+reference; here it is checked against golden vectors that
+tests/golden/make_golden.py produced by running the reference's own oracle, and
+against the reference's known answers.
+"""
+import numpy as np
+import pytest
+
+import inputs
+from oracle import afa_oracle as orc
+
+
+def test_golden_inputs_regenerate(golden_meta):
+    """Seeded inputs are bit-identical to the ones the fixtures were made from."""
+    want = golden_meta["input_sha256"]
+    assert inputs.digest(inputs.octic_grid()) == want["octic_grid"]
+    assert inputs.digest(inputs.softmax_rows()) == want["softmax_rows"]
+    assert inputs.digest(inputs.softmax_long_rows()) == want["softmax_long_rows"]
+    assert inputs.digest(*inputs.afa_small()) == want["afa_small"]
+    assert inputs.digest(*inputs.afa_l180()) == want["afa_l180"]
+    assert inputs.digest(*inputs.config1()) == want["config1"]
+    assert inputs.digest(*inputs.decode_small()) == want["decode_small"]
+
+
+def test_octic_matches_reference_kernel(golden):
+    np.testing.assert_allclose(orc.octic(inputs.octic_grid()), golden["octic_y"], rtol=1e-15, atol=0)
+
+
+def test_octic_known_answers():
+    # tests/test_attention.py:33-34 of the reference
+    np.testing.assert_allclose(orc.octic(2.0), 51841 + 23184 * np.sqrt(5), rtol=2e-15)
+    assert orc.octic(3.0) / orc.octic(-3.0) > 1e5
+    # rho(x) * rho(-x) = 1 exactly in exact arithmetic
+    x = np.linspace(0.0, 30.0, 301)
+    np.testing.assert_allclose(orc.octic(x) * orc.octic(-x), 1.0, rtol=1e-12)
+    # negative tail stays positive and finite (tests/test_pallas_afa.py:90-96)
+    tail = orc.octic(np.array([-1e2, -1e3, -1e4]))
+    assert np.all(tail > 0) and np.all(np.isfinite(tail))
+
+
+@pytest.mark.parametrize("sink", [0.0, 0.5, 1.0])
+def test_attention_matches_reference(golden, sink):
+    np.testing.assert_allclose(orc.attention(inputs.softmax_rows(), sink), golden[f"asm_y_sink{sink}"],
+                               rtol=1e-14, atol=1e-300)
+
+
+def test_attention_long_rows(golden):
+    y = orc.attention(inputs.softmax_long_rows(), 0.5)
+    np.testing.assert_allclose(y, golden["asm_long_y"], rtol=2e-7, atol=1e-30)
+
+
+def test_afa_matches_reference(golden):
+    q, k, v = inputs.afa_small()
+    assert orc.rel_err(orc.afa(q, k, v, causal=False), golden["afa_small_y"]) <= 1e-13
+    assert orc.rel_err(orc.afa(q, k, v, causal=True), golden["afa_small_y_causal"]) <= 1e-13
+
+
+def test_afa_ragged_and_config1(golden):
+    q, k, v = inputs.afa_l180()
+    assert orc.rel_err(orc.afa(q, k, v), golden["afa_l180_y"]) <= 1e-6
+    assert orc.rel_err(orc.afa(q, k, v, causal=True), golden["afa_l180_y_causal"]) <= 1e-6
+    q, k, v = inputs.config1()
+    assert orc.rel_err(orc.afa(q, k, v), golden["cfg1_afa_o"]) <= 1e-6
+    s = np.matmul(q.astype(np.float64), np.swapaxes(k.astype(np.float64), -1, -2)) / np.sqrt(q.shape[-1])
+    o = np.matmul(orc.attention(s, 0.5, 1e-5), v.astype(np.float64))
+    assert orc.rel_err(o, golden["cfg1_softmax_o"]) <= 1e-6
+
+
+def test_decode_matches_reference(golden):
+    q, k, v = inputs.decode_small()
+    out, den = orc.decode(q, k, v)
+    assert orc.rel_err(out, golden["dec_y"]) <= 1e-13
+    assert den.shape == (2, 4, 1, 1)
+
+
+@pytest.mark.parametrize("causal", [False, True])
+def test_blocked_equals_full(causal):
+    rng = np.random.default_rng(3)
+    q, k, v = (rng.normal(size=(1, 2, 300, 16)) for _ in range(3))
+    full, den = orc.afa_with_denominator(q, k, v, causal=causal)
+    blk, bden = orc.afa_blocked(q, k, v, causal=causal, block=64)
+    assert orc.rel_err(blk, full) <= 1e-13
+    assert orc.rel_err(bden, den) <= 1e-13
+
+
+def test_blocked_valid_len_and_positions():
+    rng = np.random.default_rng(4)
+    q, k, v = (rng.normal(size=(1, 1, 64, 8)) for _ in range(3))
+    out, _ = orc.afa_blocked(q, k, v, valid_len=40)
+    ref = orc.afa(q, k[..., :40, :], v[..., :40, :])
+    assert orc.rel_err(out, ref) <= 1e-13
+    # shifting every position by the same offset changes nothing
+    a, _ = orc.afa_blocked(q, k, v, causal=True)
+    b, _ = orc.afa_blocked(q, k, v, causal=True, q_pos0=1000, k_pos0=1000)
+    assert orc.rel_err(a, b) == 0.0
+
+
+@pytest.mark.parametrize("world", [2, 3, 4])
+@pytest.mark.parametrize("causal", [False, True])
+@pytest.mark.parametrize("zigzag", [False, True])
+def test_ring_simulation_equals_global(world, causal, zigzag):
+    """The reference's ring-equivalence property (tests/test_pallas_afa.py:227-271)."""
+    rng = np.random.default_rng(107)
+    q, k, v = (rng.normal(size=(1, 2, 24 * world, 8)) for _ in range(3))
+    ring = orc.ring_simulation(q, k, v, world, causal=causal, zigzag=zigzag)
+    assert orc.rel_err(ring, orc.afa(q, k, v, causal=causal)) <= 1e-12
