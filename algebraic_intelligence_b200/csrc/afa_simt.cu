@@ -23,6 +23,14 @@ __device__ __forceinline__ A octic_simt(A s) {
   return octic_ref(s);
 }
 
+// Accumulator of the P.V numerator and the row sum. Float32 inputs accumulate
+// in float64 here: the result is then the correctly rounded float32 of a
+// nearly exact sum, so the single-device forward and a ring that splits the
+// same sum over hops agree to one float32 rounding per hop.
+template <typename T> struct SumOf { using type = float; };
+template <> struct SumOf<float> { using type = double; };
+template <> struct SumOf<double> { using type = double; };
+
 template <typename T, typename A>
 __device__ __forceinline__ A round_p(A p) {
   if constexpr (sizeof(A) == 8) {
@@ -69,13 +77,14 @@ __global__ void __launch_bounds__(256) afa_simt_fwd_kernel(const __grid_constant
   const int last = min(r0 + BM - 1, P.q.len - 1);
   const int qpos_first = P.q.pos0 + r0;
 
-  A o[TR][OC];
-  A rs[TR];
+  using W = typename SumOf<T>::type;
+  W o[TR][OC];
+  W rs[TR];
 #pragma unroll
   for (int i = 0; i < TR; ++i) {
-    rs[i] = A(0);
+    rs[i] = W(0);
 #pragma unroll
-    for (int j = 0; j < OC; ++j) o[i][j] = A(0);
+    for (int j = 0; j < OC; ++j) o[i][j] = W(0);
   }
 
   for (int s = 0; s < P.nk; ++s) {
@@ -124,21 +133,21 @@ __global__ void __launch_bounds__(256) afa_simt_fwd_kernel(const __grid_constant
             const bool vis = (kbase + c < ks.len) && (!L.causal || kpos0 + c <= qpos);
             p = vis ? p : A(0);
           }
-          rs[i] += p;
+          rs[i] += static_cast<W>(p);
           Ps[(ty + 16 * i) * PLD + c] = round_p<T, A>(p);
         }
       }
       __syncthreads();
 #pragma unroll 4
       for (int kk = 0; kk < BN; ++kk) {
-        A pv[TR];
+        W pv[TR];
 #pragma unroll
-        for (int i = 0; i < TR; ++i) pv[i] = Ps[(ty + 16 * i) * PLD + kk];
+        for (int i = 0; i < TR; ++i) pv[i] = static_cast<W>(Ps[(ty + 16 * i) * PLD + kk]);
 #pragma unroll
         for (int j = 0; j < OC; ++j) {
           const int col = tx + 16 * j;
           if (col < D) {
-            const A vv = Vs[kk * LD + col];
+            const W vv = static_cast<W>(Vs[kk * LD + col]);
 #pragma unroll
             for (int i = 0; i < TR; ++i) o[i][j] = fma(pv[i], vv, o[i][j]);
           }
@@ -161,23 +170,23 @@ __global__ void __launch_bounds__(256) afa_simt_fwd_kernel(const __grid_constant
     if (rl >= P.q.len) continue;
     const long long grow = static_cast<long long>(bh) * L.lq + P.q.row0 + rl;
     A* arow = static_cast<A*>(L.o_acc) + grow * D;
-    const A drow = rs[i] + (add_prev ? static_cast<const A*>(L.d_acc)[grow] : A(0));
-    const A denom = drow + sink;
+    const W drow = rs[i] + (add_prev ? static_cast<W>(static_cast<const A*>(L.d_acc)[grow]) : W(0));
+    const W denom = drow + static_cast<W>(sink);
 #pragma unroll
     for (int j = 0; j < OC; ++j) {
       const int col = tx + 16 * j;
       if (col >= D) continue;
-      const A x = o[i][j] + (add_prev ? arow[col] : A(0));
+      const W x = o[i][j] + (add_prev ? static_cast<W>(arow[col]) : W(0));
       if (fin)
-        static_cast<T*>(L.out)[grow * D + col] = from_acc<T>(x / denom);
+        static_cast<T*>(L.out)[grow * D + col] = from_acc<T>(static_cast<A>(x / denom));
       else
-        arow[col] = x;
+        arow[col] = static_cast<A>(x);
     }
     if (tx == 0) {
       if (fin) {
-        if (L.dtot) static_cast<A*>(L.dtot)[grow] = denom;
+        if (L.dtot) static_cast<A*>(L.dtot)[grow] = static_cast<A>(denom);
       } else {
-        static_cast<A*>(L.d_acc)[grow] = drow;
+        static_cast<A*>(L.d_acc)[grow] = static_cast<A>(drow);
       }
     }
   }

@@ -45,6 +45,7 @@ RING = dict(B=1, H=16, L=65536, D=128)
 CFG3 = dict(B=2, H=32, L=4096, D=128)
 CFG2 = dict(B=4, H=16, L=2048, D=128)
 DEC = dict(B=64, H=32, L=8192, D=128)
+DEC_SMALL = dict(B=8, H=32, L=8192, D=128)  # profiling size (about 1 GB per input set)
 
 
 def causal_flops(B, H, L, D, **_):
@@ -362,10 +363,10 @@ def run_prefill(cfg, args, peaks, outliers=False):
                          "frac": ach / peaks["bf16_tflops"], "peak_source": peaks["source"] + " bf16_tflops"}}
 
 
-def run_decode(args, peaks):
+def run_decode(args, peaks, cfg=DEC):
     import torch
     import algebraic_intelligence_b200 as afa
-    B, H, L, D = DEC["B"], DEC["H"], DEC["L"], DEC["D"]
+    B, H, L, D = cfg["B"], cfg["H"], cfg["L"], cfg["D"]
     gen = torch.Generator(device="cuda").manual_seed(0)
     sets = []
     for _ in range(2):
@@ -470,7 +471,7 @@ def main():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="all", choices=["all", "ring", "prefill3", "prefill2", "decode"],
+    ap.add_argument("--workload", default="all", choices=["all", "ring", "prefill3", "prefill2", "decode", "decode_small"],
                     help="profiling aid: run one workload only (N=1)")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     args = ap.parse_args()
@@ -491,7 +492,8 @@ def main():
         fn = {"ring": lambda: run_ring(args, rank, world, peaks, traffic),
               "prefill3": lambda: run_prefill(CFG3, args, peaks),
               "prefill2": lambda: run_prefill(CFG2, args, peaks, outliers=True),
-              "decode": lambda: run_decode(args, peaks)}[args.workload]
+              "decode": lambda: run_decode(args, peaks),
+              "decode_small": lambda: run_decode(args, peaks, DEC_SMALL)}[args.workload]
         res = fn()
         if rank == 0:
             print(json.dumps({"workload": args.workload, **res}), flush=True)
