@@ -9,21 +9,30 @@
 // and finishes with O / (d + sink) and d_total = d + sink (:142-151). There is
 // no running maximum, so tiles add up with no rescaling.
 //
-// B200 design (one CTA per SM, 384 threads, two 128-row query tiles per CTA):
-//   warp 0      TMA producer: Q once, then K_j / V_j tiles through a ring of
+// B200 design (one CTA per SM, 576 threads, two 128-row query tiles per CTA):
+//   warp 16     TMA producer: Q once, then K_j / V_j tiles through a ring of
 //               shared-memory slots (128-byte swizzle, no multicast).
-//   warp 1      allocates 512 TMEM columns and issues every tcgen05.mma from one
+//   warp 17     allocates 512 TMEM columns and issues every tcgen05.mma from one
 //               thread: S_i = Q_i K_j^T (A, B from shared memory) and
-//               O_i += P_i V_j (A = P from TMEM, B = V from shared memory).
-//   warps 4-7   "softmax" group of query tile 0, warps 8-11 of tile 1: each
-//               thread owns one query row (one TMEM lane), reads its S row,
-//               applies the octic map and masks in registers, keeps the fp32
-//               row sum, and writes P as packed bf16 back over the first 64
-//               columns of its S tile. The two groups alternate with the tensor
-//               core (while group 0 maps S_0, the MMA pipe runs tile 1).
-//   epilogue    the same groups read O from TMEM, divide once by (d + sink) and
-//               store bf16 rows (or add the raw numerator / row sum into fp32
-//               accumulators for ring hops).
+//               O_i += P_i V_j (A = P from TMEM, B = V from shared memory), in
+//               the order PV_0(t) S_0(t+1) PV_1(t) S_1(t+1). The tensor core
+//               accepts only about two instructions ahead of the one executing,
+//               so the issuer waits for the K/V fills of an iteration up front
+//               and then issues each tile's 16 instructions back to back.
+//   warps 0-15  four "octic" warpgroups. Warpgroup g owns key columns
+//               [32g, 32g+32) of both query tiles and maps tile 0, then tile 1,
+//               then the next S of tile 0, ... Each thread owns one query row
+//               (one TMEM lane): it reads its 32 scores, applies the octic map
+//               and masks in registers, keeps fp32 partial row sums, and writes
+//               P as packed bf16 to TMEM columns [32g, 32g+16) of the tile's S
+//               region. All 16 warps work on the tile whose S just landed, so
+//               the map of one tile (the critical path the tensor core waits
+//               on) runs at the SM's MUFU/FMA throughput, while the tensor core
+//               computes the other tile's P.V and next S.
+//   epilogue    the four row-sum partials meet once in shared memory; each
+//               warpgroup reads its quarter of O's columns from TMEM, divides
+//               once by (d + sink) and stores bf16 (or stores / adds /
+//               adds-and-divides the fp32 ring accumulators).
 // TMEM columns: S0/P0 [0,128), S1/P1 [128,256), O0 [256,256+D), O1 [256+D, ...).
 #include <cuda.h>
 #include <cudaTypedefs.h>
@@ -36,7 +45,10 @@ namespace {
 
 template <int HD>
 struct TcCfg {
-  static constexpr int kThreads = 384;
+  static constexpr int kOcticWarps = 16;
+  static constexpr int kTmaWarp = 16;
+  static constexpr int kMmaWarp = 17;
+  static constexpr int kThreads = 18 * 32;
   static constexpr int BM = 128;
   static constexpr int BN = 128;
   static constexpr int KSUB = HD / 64;             // 64-element (128 B) column blocks
@@ -47,10 +59,16 @@ struct TcCfg {
   static constexpr int KV_OFF = 2 * TILE_BYTES;
   static constexpr int BAR_OFF = KV_OFF + NSLOT * TILE_BYTES;
   static constexpr int NBAR = 1 + 2 * NSLOT + 2 + 2 + 2 + 1;
-  static constexpr int SMEM_BYTES = BAR_OFF + NBAR * 8 + 16 + 1024;
+  static constexpr int RED_OFF = BAR_OFF + NBAR * 8 + 16;  // fp32 row-sum partials [tile][warpgroup][row]
+  static constexpr int SMEM_BYTES = RED_OFF + 2 * 4 * 128 * 4 + 1024;
   static constexpr uint32_t TMEM_COLS = 512;
   __device__ static constexpr uint32_t s_col(int i) { return static_cast<uint32_t>(i) * 128u; }
   __device__ static constexpr uint32_t o_col(int i) { return 256u + static_cast<uint32_t>(i) * HD; }
+  // P of keys [16kk, 16kk+16): warpgroup g packs keys [32g, 32g+32) into
+  // columns [32g, 32g+16), 8 columns per 16 keys.
+  __device__ static constexpr uint32_t p_col(int kk) {
+    return static_cast<uint32_t>((kk >> 1) * 32 + (kk & 1) * 8);
+  }
 };
 
 // Key tiles of one segment visible from a query tile whose last valid row sits
@@ -83,31 +101,31 @@ __device__ __forceinline__ KvTile kv_tile(const Problem& P, int cnt_seg0, int t)
 }
 
 // Octic map of one 32-column chunk of a score row, written back as 16 packed
-// bf16 pairs. MASK selects the per-element visibility test.
+// bf16 pairs; returns the chunk's fp32 row sum. MASK selects the per-element
+// visibility test (diagonal and partial tiles only).
 template <bool MASK>
 __device__ __forceinline__ float map_chunk(const uint32_t (&sv)[32], uint32_t (&pk)[16], float scale, int key0,
                                            int lim, int causal, int kpos0, int qpos) {
-  float a0 = 0.f, a1 = 0.f;
+  float2 acc = make_float2(0.f, 0.f);
+  const float2 sc = make_float2(scale, scale);
 #pragma unroll
   for (int e = 0; e < 32; e += 2) {
-    float p0 = octic_fast(__uint_as_float(sv[e]) * scale);
-    float p1 = octic_fast(__uint_as_float(sv[e + 1]) * scale);
+    float2 p = octic_fast2(__fmul2_rn(make_float2(__uint_as_float(sv[e]), __uint_as_float(sv[e + 1])), sc));
     if (MASK) {
       const int c0 = key0 + e, c1 = c0 + 1;
       const bool v0 = (c0 < lim) && (!causal || kpos0 + c0 <= qpos);
       const bool v1 = (c1 < lim) && (!causal || kpos0 + c1 <= qpos);
-      p0 = v0 ? p0 : 0.f;
-      p1 = v1 ? p1 : 0.f;
+      p.x = v0 ? p.x : 0.f;
+      p.y = v1 ? p.y : 0.f;
     }
-    a0 += p0;
-    a1 += p1;
-    pk[e >> 1] = pack_bf16x2(p0, p1);
+    acc = __fadd2_rn(acc, p);
+    pk[e >> 1] = pack_bf16x2(p.x, p.y);
   }
-  return a0 + a1;
+  return acc.x + acc.y;
 }
 
 template <int HD>
-__global__ void __launch_bounds__(384, 1)
+__global__ void __launch_bounds__(576, 1)
     afa_tc_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                       const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ Launch L) {
   using C = TcCfg<HD>;
@@ -122,6 +140,7 @@ __global__ void __launch_bounds__(384, 1)
   uint64_t* o_full = p_full + 2;
   uint64_t* drain = o_full + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  float* red = reinterpret_cast<float*>(smem + C::RED_OFF);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -160,7 +179,7 @@ __global__ void __launch_bounds__(384, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(s_full + i, 1);
-      mbar_init(p_full + i, 128);
+      mbar_init(p_full + i, 16);  // one elected arrive per octic warp
       mbar_init(o_full + i, 1);
     }
     mbar_init(drain, 1);
@@ -170,7 +189,7 @@ __global__ void __launch_bounds__(384, 1)
     prefetch_tmap(&tm_k);
     prefetch_tmap(&tm_v);
   }
-  if (warp == 1) {
+  if (warp == C::kMmaWarp) {
     tmem_alloc(tmem_slot, C::TMEM_COLS);
     tmem_relinquish();
   }
@@ -179,7 +198,7 @@ __global__ void __launch_bounds__(384, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 0) {
+  if (warp == C::kTmaWarp) {
     // ------------------------------------------------------------------ TMA
     if (lane == 0 && n1 > 0) {
       mbar_arrive_expect_tx(q_full, 2 * C::TILE_BYTES);
@@ -211,7 +230,7 @@ __global__ void __launch_bounds__(384, 1)
       for (int u = issued - C::NSLOT < 0 ? 0 : issued - C::NSLOT; u < issued; ++u)
         (void)mbar_wait(kv_full + (u % C::NSLOT), (u / C::NSLOT) & 1, nullptr, 0);
     }
-  } else if (warp == 1) {
+  } else if (warp == C::kMmaWarp) {
     // ------------------------------------------------------------------ MMA
     if (lane == 0 && n1 > 0) {
       constexpr uint32_t idesc_s = idesc_bf16_f32(128, 128, false);
@@ -231,7 +250,7 @@ __global__ void __launch_bounds__(384, 1)
 #pragma unroll
         for (int kk = 0; kk < C::BN / 16; ++kk) {
           const uint64_t b = sw128_desc(kv_base + slot * C::TILE_BYTES + kk * 2048, C::SUB_BYTES, 1024);
-          umma_ts(tmem + C::o_col(i), tmem + C::s_col(i) + kk * 8, b, idesc_o, (acc || kk > 0) ? 1u : 0u);
+          umma_ts(tmem + C::o_col(i), tmem + C::s_col(i) + C::p_col(kk), b, idesc_o, (acc || kk > 0) ? 1u : 0u);
         }
       };
       bool ok = mbar_wait(q_full, 0, L.status, kDevTimeoutMma) && mbar_wait(kv_full + 0, 0, L.status, kDevTimeoutMma);
@@ -247,20 +266,18 @@ __global__ void __launch_bounds__(384, 1)
       }
       for (int t = 0; ok && t < n1; ++t) {
         const int uv = 2 * t + 1, sv = uv % C::NSLOT;
+        const int uk = 2 * t + 2, sk = uk % C::NSLOT;
+        const bool more = t + 1 < n1;
+        // Both fills of this iteration first (usually long complete), so the
+        // only wait left between instruction blocks is the P dependency.
         if (!(ok = mbar_wait(kv_full + sv, (uv / C::NSLOT) & 1, L.status, kDevTimeoutMma))) break;
-        tc_fence_after();
+        if (more && !(ok = mbar_wait(kv_full + sk, (uk / C::NSLOT) & 1, L.status, kDevTimeoutMma))) break;
         if (t < n0) {
           if (!(ok = mbar_wait(p_full + 0, t & 1, L.status, kDevTimeoutMma))) break;
           tc_fence_after();
           issue_o(0, sv, t > 0);
           if (t + 1 == n0) umma_commit(o_full + 0);
-        }
-        const bool more = t + 1 < n1;
-        const int uk = 2 * t + 2, sk = uk % C::NSLOT;
-        if (more) {
-          if (!(ok = mbar_wait(kv_full + sk, (uk / C::NSLOT) & 1, L.status, kDevTimeoutMma))) break;
-          tc_fence_after();
-          if (t + 1 < n0) {
+          if (more && t + 1 < n0) {
             issue_s(0, sk);
             umma_commit(s_full + 0);
           }
@@ -280,120 +297,137 @@ __global__ void __launch_bounds__(384, 1)
       umma_commit(drain);
       (void)mbar_wait(drain, 0, nullptr, 0);
     }
-  } else if (warp >= 4) {
+  } else {
     // --------------------------------------------------- octic map + epilogue
-    const int wg = (warp - 4) >> 2;
-    const int sub = warp & 3;
+    const int g = warp >> 2;           // warpgroup: key columns [32g, 32g+32)
+    const int sub = warp & 3;          // TMEM lane quarter
     const int row = sub * 32 + lane;
-    const int rloc = r0 + 128 * wg + row;
-    const int qpos = P.q.pos0 + rloc;
-    const int qfirst = P.q.pos0 + r0 + 128 * wg;
     const uint32_t lane_off = static_cast<uint32_t>(sub * 32) << 16;
-    const uint32_t s_tm = tmem + C::s_col(wg) + lane_off;
-    const uint32_t o_tm = tmem + C::o_col(wg) + lane_off;
-    const int n = wg ? n1 : n0;
     const float scale = L.scale;
-    float dsum = 0.f;
+    float dsum[2] = {0.f, 0.f};
     bool ok = true;
-    for (int t = 0; t < n; ++t) {
-      ok = mbar_wait(s_full + wg, t & 1, L.status, kDevTimeoutSoftmax);
-      ok = __all_sync(0xffffffffu, ok);
-      if (!ok) break;
-      tc_fence_after();
+    for (int t = 0; t < n1 && ok; ++t) {
       const KvTile kt = kv_tile(P, cnt1[0], t);
-      const bool need_mask = kt.lim < 128 || (L.causal && kt.pos + 127 > qfirst);
-      float part = 0.f;
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
+      for (int tile = 0; tile < 2; ++tile) {
+        if (tile == 0 && t >= n0) continue;
+        ok = mbar_wait(s_full + tile, t & 1, L.status, kDevTimeoutSoftmax);
+        ok = __all_sync(0xffffffffu, ok);
+        if (!ok) break;
+        tc_fence_after();
+        const int qfirst = P.q.pos0 + r0 + 128 * tile;
+        const int qpos = qfirst + row;
+        const bool need_mask = kt.lim < 128 || (L.causal && kt.pos + 127 > qfirst);
+        const uint32_t s_tm = tmem + C::s_col(tile) + lane_off + 32 * g;
         uint32_t sv[32];
         uint32_t pk[16];
-        tmem_ld32(s_tm + 32 * c, sv);
+        tmem_ld32(s_tm, sv);
         tmem_ld_wait();
-        if (need_mask)
-          part += map_chunk<true>(sv, pk, scale, 32 * c, kt.lim, L.causal, kt.pos, qpos);
-        else
-          part += map_chunk<false>(sv, pk, scale, 32 * c, kt.lim, L.causal, kt.pos, qpos);
-        tmem_st16(s_tm + 16 * c, pk);
-      }
-      tmem_st_wait();
-      tc_fence_before();
-      mbar_arrive(p_full + wg);
-      dsum += part;
-    }
-    bool have_o = false;
-    if (ok && n > 0) {
-      ok = mbar_wait(o_full + wg, 0, L.status, kDevTimeoutEpilogue);
-      ok = __all_sync(0xffffffffu, ok);
-      if (ok) {
-        tc_fence_after();
-        have_o = true;
+        const float part = need_mask ? map_chunk<true>(sv, pk, scale, 32 * g, kt.lim, L.causal, kt.pos, qpos)
+                                     : map_chunk<false>(sv, pk, scale, 32 * g, kt.lim, L.causal, kt.pos, qpos);
+        // P of these 32 keys -> the first 16 of the 32 columns just read.
+        tmem_st16(s_tm, pk);
+        // Every lane's P stores are complete (wait::st) and ordered before the
+        // warp's single arrive.
+        tmem_st_wait();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(p_full + tile);
+        dsum[tile] += part;
       }
     }
-    const bool row_ok = rloc < P.q.len;
-    const long long grow = static_cast<long long>(bh) * L.lq + P.q.row0 + rloc;
+    bool have_o[2] = {false, false};
+#pragma unroll
+    for (int tile = 0; tile < 2; ++tile) {
+      const int n = tile ? n1 : n0;
+      if (ok && n > 0) {
+        ok = mbar_wait(o_full + tile, 0, L.status, kDevTimeoutEpilogue);
+        ok = __all_sync(0xffffffffu, ok);
+        have_o[tile] = ok;
+      }
+      red[(tile * 4 + g) * 128 + row] = dsum[tile];
+    }
+    tc_fence_after();
+    // The four column partials of every row meet here (fixed order g = 0..3).
+    asm volatile("bar.sync 1, %0;" ::"r"(C::kOcticWarps * 32) : "memory");
+
     const bool fin = L.mode == kFinal || L.mode == kAccumFinal;
     const bool add_prev = L.mode == kAccumRaw || L.mode == kAccumFinal;
-    float* acc_row = fin && !add_prev ? nullptr : static_cast<float*>(L.o_acc) + grow * HD;
-    const float dprev = (row_ok && add_prev) ? static_cast<const float*>(L.d_acc)[grow] : 0.f;
-    const float drow = dsum + dprev;
-    const float denom = drow + L.sink;
-    const float inv = 1.0f / denom;
-    __nv_bfloat16* orow = static_cast<__nv_bfloat16*>(L.out) + grow * HD;
+    constexpr int OC = HD / 4;  // O columns per warpgroup: 32 (D=128) or 16 (D=64)
 #pragma unroll
-    for (int c = 0; c < HD / 32; ++c) {
+    for (int tile = 0; tile < 2; ++tile) {
+      const float drow_tile = red[(tile * 4 + 0) * 128 + row] + red[(tile * 4 + 1) * 128 + row] +
+                              red[(tile * 4 + 2) * 128 + row] + red[(tile * 4 + 3) * 128 + row];
+      const int rloc = r0 + 128 * tile + row;
+      const bool row_ok = rloc < P.q.len;
+      const long long grow = static_cast<long long>(bh) * L.lq + P.q.row0 + rloc;
+      float* acc_row = fin && !add_prev ? nullptr : static_cast<float*>(L.o_acc) + grow * HD + OC * g;
+      const float dprev = (row_ok && add_prev) ? static_cast<const float*>(L.d_acc)[grow] : 0.f;
+      const float drow = drow_tile + dprev;
+      const float denom = drow + L.sink;
+      const float inv = 1.0f / denom;
       uint32_t ov[32];
-      __syncwarp();  // tcgen05.ld is warp-collective; rows that skipped the store rejoin here
-      if (have_o) {
-        tmem_ld32(o_tm + 32 * c, ov);
+      __syncwarp();  // tcgen05.ld is warp-collective
+      if (have_o[tile]) {
+        const uint32_t o_tm = tmem + C::o_col(tile) + lane_off + OC * g;
+        if constexpr (OC == 32) {
+          tmem_ld32(o_tm, ov);
+        } else {
+          uint32_t (&ov16)[16] = *reinterpret_cast<uint32_t(*)[16]>(ov);
+          tmem_ld16(o_tm, ov16);
+        }
         tmem_ld_wait();
       } else {
 #pragma unroll
         for (int e = 0; e < 32; ++e) ov[e] = 0u;
       }
-      if (!row_ok) continue;
-      float x[32];
+      if (row_ok) {
+        float x[OC];
 #pragma unroll
-      for (int e = 0; e < 32; ++e) x[e] = __uint_as_float(ov[e]);
-      if (add_prev) {
-        const float4* src = reinterpret_cast<const float4*>(acc_row + 32 * c);
+        for (int e = 0; e < OC; ++e) x[e] = __uint_as_float(ov[e]);
+        if (add_prev) {
+          const float4* src = reinterpret_cast<const float4*>(acc_row);
 #pragma unroll
-        for (int w = 0; w < 8; ++w) {
-          const float4 y = src[w];
-          x[4 * w + 0] += y.x;
-          x[4 * w + 1] += y.y;
-          x[4 * w + 2] += y.z;
-          x[4 * w + 3] += y.w;
+          for (int w = 0; w < OC / 4; ++w) {
+            const float4 y = src[w];
+            x[4 * w + 0] += y.x;
+            x[4 * w + 1] += y.y;
+            x[4 * w + 2] += y.z;
+            x[4 * w + 3] += y.w;
+          }
         }
-      }
-      if (fin) {
-        uint4* dst = reinterpret_cast<uint4*>(orow + 32 * c);
+        if (fin) {
+          uint4* dst = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(L.out) + grow * HD + OC * g);
 #pragma unroll
-        for (int w = 0; w < 4; ++w) {
-          uint4 pkt;
-          pkt.x = pack_bf16x2(x[8 * w + 0] * inv, x[8 * w + 1] * inv);
-          pkt.y = pack_bf16x2(x[8 * w + 2] * inv, x[8 * w + 3] * inv);
-          pkt.z = pack_bf16x2(x[8 * w + 4] * inv, x[8 * w + 5] * inv);
-          pkt.w = pack_bf16x2(x[8 * w + 6] * inv, x[8 * w + 7] * inv);
-          dst[w] = pkt;
+          for (int w = 0; w < OC / 8; ++w) {
+            uint4 pkt;
+            pkt.x = pack_bf16x2(x[8 * w + 0] * inv, x[8 * w + 1] * inv);
+            pkt.y = pack_bf16x2(x[8 * w + 2] * inv, x[8 * w + 3] * inv);
+            pkt.z = pack_bf16x2(x[8 * w + 4] * inv, x[8 * w + 5] * inv);
+            pkt.w = pack_bf16x2(x[8 * w + 6] * inv, x[8 * w + 7] * inv);
+            dst[w] = pkt;
+          }
+        } else {
+          float4* dst = reinterpret_cast<float4*>(acc_row);
+#pragma unroll
+          for (int w = 0; w < OC / 4; ++w) dst[w] = make_float4(x[4 * w + 0], x[4 * w + 1], x[4 * w + 2], x[4 * w + 3]);
         }
-      } else {
-        float4* dst = reinterpret_cast<float4*>(acc_row + 32 * c);
-#pragma unroll
-        for (int w = 0; w < 8; ++w) dst[w] = make_float4(x[4 * w + 0], x[4 * w + 1], x[4 * w + 2], x[4 * w + 3]);
-      }
-    }
-    if (row_ok) {
-      if (fin) {
-        if (L.dtot) static_cast<float*>(L.dtot)[grow] = denom;
-      } else {
-        static_cast<float*>(L.d_acc)[grow] = drow;
+        // d_acc / d_total: one writer per row (warpgroup 0); the others only
+        // read d_acc above, in kAccumFinal, where nothing writes it.
+        if (g == 0) {
+          if (fin) {
+            if (L.dtot) static_cast<float*>(L.dtot)[grow] = denom;
+          } else {
+            static_cast<float*>(L.d_acc)[grow] = drow;
+          }
+        }
       }
     }
   }
 
   tc_fence_before();
   __syncthreads();
-  if (warp == 1) {
+  if (warp == C::kMmaWarp) {
     __syncwarp();
     tc_fence_after();
     tmem_dealloc(tmem, C::TMEM_COLS);
