@@ -31,6 +31,7 @@ SIGNATURES = {
     "afa_decode": (_c_int, [_c_void_p] * 5 + [_c_int] * 5 + [_c_float, _c_void_p, _c_int, _c_void_p, _c_size,
                                                              _c_void_p]),
     "afa_decode_workspace_bytes": (_c_size, [_c_int] * 4),
+    "afa_decode_noalloc": (_c_int, [_c_void_p] * 5 + [_c_int] * 5 + [_c_float, _c_void_p, _c_int, _c_void_p]),
     "algebraic_softmax_fwd": (_c_int, [_c_void_p, _c_void_p, _c_ll, _c_int, _c_int, _c_double, _c_double,
                                        _c_void_p]),
     "afa_octic": (_c_int, [_c_void_p, _c_void_p, _c_ll, _c_int, _c_void_p]),

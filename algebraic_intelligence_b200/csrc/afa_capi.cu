@@ -97,6 +97,13 @@ int run_launch(afa::Launch& L, int dtype, cudaStream_t stream) {
 
 }  // namespace
 
+namespace afa {
+int set_last_error(int code, const char* msg) {
+  g_last_error = msg;
+  return code;
+}
+}  // namespace afa
+
 extern "C" {
 
 const char* afa_version(void) { return "afa_b200 0.1.0 sm_100a"; }

@@ -140,6 +140,23 @@ AFA_API int afa_decode(const void* q, const void* k_cache, const void* v_cache, 
 AFA_API size_t afa_decode_workspace_bytes(int B, int H, int Lkv, int D);
 
 /*
+ * Allocation-free decode step. No counterpart in the reference: it is
+ * afa_decode for callers that cannot hand over device scratch memory --
+ * code inside a CUDA graph capture, plugin hosts whose allocator belongs to
+ * another runtime, serving loops that forbid allocation per token. Same
+ * arguments and results as afa_decode minus the workspace. The split-KV
+ * scratch instead lives in a fixed 1 MiB array that every GPU loading the
+ * library keeps until exit. Shapes needing more scratch than that
+ * (afa_decode_workspace_bytes > 1 MiB) return AFA_ERR_INVALID. All calls
+ * share the array, so calls that overlap on the GPU race; serialise them on
+ * one stream. The first call on a device resolves the array's device address
+ * (cudaGetSymbolAddress); make it outside any stream capture.
+ */
+AFA_API int afa_decode_noalloc(const void* q, const void* k_cache, const void* v_cache, void* out, void* d_total,
+                               int B, int H, int Lkv, int D, int dtype, float sink_omega, const int* kv_lens,
+                               int kv_len, void* stream);
+
+/*
  * algebraic_softmax (src/attention.py:88-91): rows x cols, last axis
  * normalised. dtype AFA_F32, AFA_BF16, AFA_F16 (fp32 accumulation) or AFA_F64.
  * Errors mirror the reference: sink_omega must be finite and >= 0, eps finite
