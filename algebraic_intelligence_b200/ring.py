@@ -7,10 +7,14 @@ added to the rank's accumulators (:648-649); one divide at the end (:661). AFA
 needs no running-max rescale, so the merge is plain addition.
 
 B200 form:
-* one process per GPU; the K/V shard is packed as one (2, B, H, S, D) buffer
-  and rotated with an NCCL send/recv pair (``torch.distributed`` P2P over
-  NVLink/NVSwitch) issued *before* the hop's kernel, so the transfer of the
-  next shard overlaps the compute on the current one (double buffer);
+* one process per GPU; each call publishes the rank's K/V shard as one
+  (2, B, H, S, D) buffer that every rank maps with CUDA IPC, and hop i pulls
+  the shard of rank ``hop.src`` straight from its owner with the copy engines
+  (``CudaIpcExchange``): over NVSwitch every GPU reaches every other at full
+  bandwidth, so the shard need not pass through the ranks in between. The
+  pull for hop i+1 overlaps hop i's kernel and uses no SM; a call needs two
+  stream-ordered barriers (after the publish, at the end) instead of a
+  send/receive pair per hop;
 * a hop is one launch of the grouped forward kernel (``afa_fwd_hop``): the
   first hop stores the accumulators, middle hops add, and the last hop adds and
   divides in its epilogue -- no separate normalisation pass;
@@ -19,7 +23,7 @@ B200 form:
   fully masked (query, key) chunk pairs are skipped on the host and partially
   masked tiles are masked in-kernel on global positions. ``layout="contiguous"``
   is the reference's own sharding (rank r holds block r).
-* no collective other than the ring P2P; no TMA multicast anywhere.
+* no collective on the data path besides the two barriers; no TMA multicast anywhere.
 """
 from __future__ import annotations
 
@@ -30,7 +34,8 @@ import torch
 
 from . import _lib
 
-__all__ = ["distributed_ring_afa", "shard_sequence", "unshard_sequence", "ring_plan", "RingHop", "local_segments"]
+__all__ = ["distributed_ring_afa", "shard_sequence", "unshard_sequence", "ring_plan", "RingHop", "local_segments",
+           "ring_loop", "KVExchange", "ListExchange", "CudaIpcExchange", "get_exchange", "release_ring_buffers"]
 
 Segment = Tuple[int, int, int]  # (row0 in the local shard, length, global position of row0)
 
@@ -128,32 +133,221 @@ def ring_plan(rank: int, world: int, seq_len: int, causal: bool, layout: str) ->
     return hops
 
 
-def _p2p_rotate(send_buf: torch.Tensor, recv_buf: torch.Tensor, rank: int, world: int, group):
-    """Start the ring step: send to rank+1, receive from rank-1 (ppermute)."""
-    import torch.distributed as dist
-    ranks = dist.get_process_group_ranks(group) if group is not None else list(range(world))
-    nxt = ranks[(rank + 1) % world]
-    prv = ranks[(rank - 1) % world]
-    ops = [dist.P2POp(dist.isend, send_buf, nxt, group), dist.P2POp(dist.irecv, recv_buf, prv, group)]
-    return dist.batch_isend_irecv(ops)
+class KVExchange:
+    """How the hops of one ring call obtain their K/V shards.
 
-
-def ring_loop(q: torch.Tensor, kv: torch.Tensor, hops: List[RingHop], compute: Callable,
-              rotate: Optional[Callable]) -> None:
-    """Drive the hops: start the next rotation, compute the current hop, wait.
-
-    ``compute(hop, k, v)`` runs one hop on the current K/V; ``rotate(send,
-    recv)`` starts the transfer and returns objects with ``wait()``.
+    ``ring_loop`` drives it: ``publish`` makes this rank's shard readable by
+    every rank of the ring and returns it as a (2, B, H, S, D) tensor;
+    ``pull(src, slot)`` starts copying rank ``src``'s published shard into
+    receive slot ``slot`` (0 or 1) and returns a token; ``ready(token)`` waits
+    for that copy and returns the slot's tensor; ``finish`` ends the call.
+    Subclasses are the transports.
     """
-    bufs = [kv, torch.empty_like(kv) if len(hops) > 1 else None]
+
+    rank = 0
+
+    def publish(self, k: torch.Tensor, v: torch.Tensor) -> torch.Tensor:
+        raise NotImplementedError
+
+    def pull(self, src: int, slot: int):
+        raise NotImplementedError
+
+    def ready(self, token) -> torch.Tensor:
+        raise NotImplementedError
+
+    def finish(self) -> None:
+        pass
+
+
+class ListExchange(KVExchange):
+    """Every rank's shard already lives in this process (a ring emulated in one
+    process, rank by rank): ``shards[r]`` is rank r's (2, B, H, S, D) K/V."""
+
+    def __init__(self, rank: int, shards: Sequence[torch.Tensor]):
+        self.rank = rank
+        self.shards = list(shards)
+        self.recv = [torch.empty_like(self.shards[rank]) for _ in range(2)]
+
+    def publish(self, k, v):
+        return self.shards[self.rank]
+
+    def pull(self, src, slot):
+        self.recv[slot].copy_(self.shards[src])
+        return slot
+
+    def ready(self, token):
+        return self.recv[token]
+
+
+class CudaIpcExchange(KVExchange):
+    """The ring transport on one node: CUDA IPC mappings and copy-engine pulls.
+
+    Each rank owns one published buffer that every other rank maps once
+    (``afa_ring_export`` / ``afa_ring_open``), and two receive slots. A call
+    copies K and V into the published buffer and runs a stream-ordered barrier
+    (a one-element all-reduce on the group), after which every rank's shard is
+    readable. Hop i then pulls the shard of rank ``hop.src`` with
+    ``afa_ring_pull`` on a copy stream: the copy engines move it over NVLink
+    while hop i-1's kernel runs, and no SM is taken from the kernel. The call
+    ends with the compute stream joining the copy stream and a second barrier,
+    so no rank's stream passes the end of a call (or the next call's publish)
+    while any rank still reads its buffer -- a rank can free its memory or exit
+    once its stream is synchronised.
+
+    Ordering inside a rank: a pull into a slot waits for the kernel that last
+    read the slot (an event on the compute stream); a hop's kernel waits for its
+    pull (an event on the copy stream).
+
+    One instance serves one (group, shape, dtype, device); ``get_exchange``
+    caches them for the life of the process (``release_ring_buffers`` drops
+    them). Buffers come from PyTorch's default caching allocator, which is built
+    on cudaMalloc as CUDA IPC requires.
+    """
+
+    def __init__(self, shape, dtype: torch.dtype, device: torch.device, group=None, copy_streams: int = 1):
+        import ctypes
+
+        import torch.distributed as dist
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.device = torch.device(device)
+        lib = _lib.load()
+        kv_shape = (2,) + tuple(shape)
+        self._pub = torch.empty(kv_shape, dtype=dtype, device=self.device)          # [K, V]
+        self._recv = torch.empty((2,) + kv_shape, dtype=dtype, device=self.device)  # [slot][K, V]
+        self.nbytes = self._pub.numel() * self._pub.element_size()
+        handle = (ctypes.c_ubyte * 64)()
+        offset = ctypes.c_ulonglong(0)
+        _lib.check(lib.afa_ring_export(self._pub.data_ptr(), handle, ctypes.byref(offset)), "afa_ring_export")
+        mine = torch.tensor(list(bytes(handle)) + list(offset.value.to_bytes(8, "little")), dtype=torch.uint8,
+                            device=self.device)
+        every = [torch.empty_like(mine) for _ in range(self.world)]
+        dist.all_gather(every, mine, group=group)
+        self._bases = []
+        self._peer = []
+        for j, t in enumerate(every):
+            if j == self.rank:
+                self._peer.append(self._pub.data_ptr())
+                continue
+            raw = bytes(t.cpu().tolist())
+            base = ctypes.c_void_p()
+            _lib.check(lib.afa_ring_open(raw[:64], ctypes.byref(base)), "afa_ring_open")
+            self._bases.append(base.value)
+            self._peer.append(base.value + int.from_bytes(raw[64:72], "little"))
+        self._flag = torch.zeros(1, dtype=torch.int32, device=self.device)
+        self._copy = [torch.cuda.Stream(self.device) for _ in range(max(1, copy_streams))]
+
+    def _barrier(self):
+        import torch.distributed as dist
+        dist.all_reduce(self._flag, group=self.group)   # stream-ordered on the current stream
+
+    def publish(self, k, v):
+        self._pub[0].copy_(k)
+        self._pub[1].copy_(v)
+        self._barrier()                                 # every rank has published
+        return self._pub
+
+    def pull(self, src, slot):
+        lib = _lib.load()
+        cur = torch.cuda.current_stream(self.device)
+        released = torch.cuda.Event()
+        released.record(cur)
+        n = len(self._copy)
+        step = -(-self.nbytes // (n * 256)) * 256
+        dst0 = self._recv[slot].data_ptr()
+        src0 = self._peer[src]
+        done = []
+        for i, s in enumerate(self._copy):
+            lo = i * step
+            size = min(step, self.nbytes - lo)
+            if size <= 0:
+                break
+            s.wait_event(released)
+            _lib.check(lib.afa_ring_pull(dst0 + lo, src0 + lo, size, s.cuda_stream), "afa_ring_pull")
+            ev = torch.cuda.Event()
+            ev.record(s)
+            done.append(ev)
+        return slot, done
+
+    def ready(self, token):
+        slot, done = token
+        cur = torch.cuda.current_stream(self.device)
+        for ev in done:
+            cur.wait_event(ev)
+        return self._recv[slot]
+
+    def finish(self):
+        cur = torch.cuda.current_stream(self.device)
+        for s in self._copy:
+            cur.wait_stream(s)
+        self._barrier()                                 # every rank is done reading every buffer
+
+    def close(self) -> None:
+        """Unmaps the peers' buffers (after the device finished this rank's work;
+        the trailing barrier of the last call already waited for every peer)."""
+        lib = _lib.load()
+        torch.cuda.synchronize(self.device)
+        for b in self._bases:
+            lib.afa_ring_close(b)
+        self._bases = []
+        self._peer = []
+
+
+_EXCHANGES = {}
+
+
+def get_exchange(shape, dtype: torch.dtype, device: torch.device, group=None) -> CudaIpcExchange:
+    """The cached exchange of ``group`` for K/V shards of ``shape`` (B, H, S, D).
+    The first call for a key is collective over the group (it swaps IPC handles)."""
+    device = torch.device(device)
+    key = (id(group), tuple(shape), dtype, device.index)
+    ex = _EXCHANGES.get(key)
+    if ex is None:
+        ex = _EXCHANGES[key] = CudaIpcExchange(shape, dtype, device, group)
+    return ex
+
+
+def release_ring_buffers() -> None:
+    """Unmaps the peers' buffers and drops every cached exchange (and with them
+    the published buffers). Call it on every rank once no rank runs ring calls
+    any more."""
+    for ex in _EXCHANGES.values():
+        ex.close()
+    _EXCHANGES.clear()
+
+
+def ring_loop(k: torch.Tensor, v: torch.Tensor, hops: List[RingHop], compute: Callable,
+              exchange: Optional[KVExchange]) -> None:
+    """Drive the hops of one ring call.
+
+    ``compute(hop, k, v)`` runs one hop on that hop's K/V. Hop 0 reads this
+    rank's own shard; hop i pulls the shard of rank ``hop.src`` from its owner,
+    the pull for hop i+1 starting before hop i's compute so the two overlap
+    (two receive slots). Hops whose problems are empty (wholly masked) pull
+    nothing. With one rank (``exchange`` None) the only hop reads k and v.
+    """
+    if exchange is None:
+        for hop in hops:
+            if hop.problems:
+                compute(hop, k, v)
+        return
+    local = exchange.publish(k, v)
+    if hops and hops[0].src != exchange.rank:
+        raise ValueError("the first hop of a ring plan must read the rank's own shard")
+
+    def start(i):
+        if 0 < i < len(hops) and hops[i].problems:
+            return exchange.pull(hops[i].src, i % 2)
+        return None
+
+    pending = None
     for i, hop in enumerate(hops):
-        cur = bufs[i % 2]
-        reqs = rotate(cur, bufs[(i + 1) % 2]) if (i + 1 < len(hops)) else None
+        kv = local if i == 0 else (exchange.ready(pending) if pending is not None else None)
+        pending = start(i + 1)
         if hop.problems:
-            compute(hop, cur[0], cur[1])
-        if reqs is not None:
-            for r in reqs:
-                r.wait()
+            compute(hop, kv[0], kv[1])
+    exchange.finish()
 
 
 def distributed_ring_afa(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, sink_omega: float = 0.5,
@@ -188,7 +382,6 @@ def distributed_ring_afa(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, sink
     seq_len = s * world
     hops = ring_plan(rank, world, seq_len, causal, layout)
     q = q.contiguous()
-    kv = torch.stack([k, v]).contiguous()
     acc_dt = _lib.accum_dtype(q.dtype)
     out = torch.empty_like(q)
     den = torch.empty((b, h, s, 1), dtype=acc_dt, device=q.device)
@@ -201,10 +394,8 @@ def distributed_ring_afa(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, sink
         hop_forward(q, kk, vv, hop.problems, causal, hop.mode, o_acc=o_acc, d_acc=d_acc, out=out, d_total=den,
                     sink_omega=sink_omega)
 
-    rotate = None
-    if world > 1:
-        rotate = lambda send, recv: _p2p_rotate(send, recv, rank, world, group)  # noqa: E731
-    ring_loop(q, kv, hops, compute, rotate)
+    exchange = get_exchange(q.shape, q.dtype, q.device, group) if world > 1 else None
+    ring_loop(k.contiguous(), v.contiguous(), hops, compute, exchange)
     if return_denominator:
         return out, den
     return out

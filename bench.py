@@ -3,8 +3,8 @@
 
 Workload at every N (so per-N values compare like with like): BASELINE config 5,
 ring AFA forward, B=1, H=16, L=65536, D=128, bf16, causal, the sequence
-zigzag-sharded over N GPUs (one process per GPU, K/V rotated with NCCL
-send/recv). At N=1 it is the single-GPU prefill forward of the whole sequence,
+zigzag-sharded over N GPUs (one process per GPU; each hop pulls its K/V shard
+from the owning GPU with the copy engines over NVLink, through CUDA IPC). At N=1 it is the single-GPU prefill forward of the whole sequence,
 the largest single-GPU configuration of BASELINE.json.
 
   metric  "AFA fwd TFLOP/s": FLOPs = 4*B*H*D*L(L+1)/2 (QK^T and PV over the
@@ -248,27 +248,24 @@ def run_ring(args, rank, world, peaks, traffic):
             f = lambda: afa.pallas_afa_forward(q, k, v, causal=True)  # noqa: E731
             kt.around(f) if kt else f()
     else:
-        import torch.distributed as dist
-        from algebraic_intelligence_b200.ring import _p2p_rotate, ring_loop
+        from algebraic_intelligence_b200.ring import get_exchange, ring_loop
         q0 = sets[0][0]
         b, h, s, d = q0.shape
         o_acc = torch.empty((b, h, s, d), dtype=torch.float32, device="cuda")
         d_acc = torch.empty((b, h, s), dtype=torch.float32, device="cuda")
         den = torch.empty((b, h, s, 1), dtype=torch.float32, device="cuda")
         out = torch.empty_like(q0)
-        kvs = [torch.stack([kk, vv]).contiguous() for _, kk, vv in sets]
-        spare = torch.empty_like(kvs[0])
+        exchange = get_exchange(q0.shape, q0.dtype, q0.device)   # the one distributed_ring_afa uses
 
         def step(i, kt):
-            q = sets[i % 2][0]
-            kv = kvs[i % 2]
+            q, k, v = sets[i % 2]
 
             def compute(hop, kk, vv):
                 f = lambda: hop_forward(q, kk, vv, hop.problems, True, hop.mode, o_acc=o_acc,  # noqa: E731
                                         d_acc=d_acc, out=out, d_total=den, sink_omega=0.5)
                 kt.around(f) if kt else f()
 
-            ring_loop_fixed(q, kv, spare, hops, compute, lambda sb, rb: _p2p_rotate(sb, rb, rank, world, None))
+            ring_loop(k, v, hops, compute, exchange)
 
     ms, kt = timed(step, args.steps, args.warmup, world)
     value = flops * args.steps / (ms / 1e3) / 1e12
@@ -288,19 +285,6 @@ def run_ring(args, rank, world, peaks, traffic):
     }
     del sets
     return res
-
-
-def ring_loop_fixed(q, kv, spare, hops, compute, rotate):
-    """ring_loop with a preallocated second K/V buffer (no allocation per step)."""
-    bufs = [kv, spare]
-    for i, hop in enumerate(hops):
-        cur = bufs[i % 2]
-        reqs = rotate(cur, bufs[(i + 1) % 2]) if i + 1 < len(hops) else None
-        if hop.problems:
-            compute(hop, cur[0], cur[1])
-        if reqs is not None:
-            for r in reqs:
-                r.wait()
 
 
 def run_ring_e2e(args, rank, world):

@@ -121,6 +121,33 @@ AFA_API int afa_finalize(const void* o_acc, const void* d_acc, void* out, void* 
                  float sink_omega, void* stream);
 
 /*
+ * Ring K/V exchange between the processes of one node (the transport that
+ * replaces lax.ppermute in distributed_ring_afa, pallas_afa.py:651-652).
+ *
+ * Each rank publishes its K/V shard in a device buffer that every other rank
+ * maps with CUDA IPC; a hop then pulls the shard it needs straight from the
+ * owning rank with the copy engines over NVLink, so the transfer uses no SMs
+ * and overlaps the previous hop's kernel. Ordering between ranks (publish
+ * before pull, pull before overwrite) is the caller's: the Python ring inserts
+ * one stream-ordered barrier per call.
+ *
+ *   afa_ring_export  IPC handle (AFA_RING_HANDLE_BYTES bytes, written to
+ *                    handle_out) of the device allocation that holds ptr, and
+ *                    ptr's byte offset in it. ptr must come from cudaMalloc (or
+ *                    an allocator built on it, like PyTorch's default one).
+ *   afa_ring_open    maps a peer's handle into this process on the current
+ *                    device; *base_out is the mapping's base (add the offset).
+ *   afa_ring_close   unmaps a base returned by afa_ring_open.
+ *   afa_ring_pull    stream-ordered copy of `bytes` from src (a peer mapping
+ *                    or local memory) to dst on the copy engines.
+ */
+#define AFA_RING_HANDLE_BYTES 64
+AFA_API int afa_ring_export(const void* ptr, void* handle_out, unsigned long long* offset_out);
+AFA_API int afa_ring_open(const void* handle, void** base_out);
+AFA_API int afa_ring_close(void* base);
+AFA_API int afa_ring_pull(void* dst, const void* src, size_t bytes, void* stream);
+
+/*
  * Decode step (no reference counterpart; the math of pallas_afa_forward with a
  * single query row, non-causal).
  *   q           (B, H, D) -- one token per (batch, head)

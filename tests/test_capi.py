@@ -90,3 +90,21 @@ def test_decode_workspace_query():
     n = lib.afa_decode_workspace_bytes(1, 1, 65536, 128)
     assert n > 0 and n % (129 * 4) == 0
     assert lib.afa_decode_workspace_bytes(0, 1, 1, 1) == 0
+
+
+def test_ring_exchange_argument_checks():
+    """The ring exchange entry points reject null pointers before any CUDA
+    call; a zero-byte pull is a no-op."""
+    import ctypes
+    lib = _lib.load()
+    handle = (ctypes.c_ubyte * 64)()
+    off = ctypes.c_ulonglong(0)
+    base = ctypes.c_void_p()
+    assert lib.afa_ring_export(None, handle, ctypes.byref(off)) == _lib.AFA_ERR_INVALID
+    assert b"afa_ring_export" in lib.afa_last_error()
+    assert lib.afa_ring_open(None, ctypes.byref(base)) == _lib.AFA_ERR_INVALID
+    assert lib.afa_ring_open(handle, None) == _lib.AFA_ERR_INVALID
+    assert lib.afa_ring_close(None) == _lib.AFA_ERR_INVALID
+    assert lib.afa_ring_pull(None, 1, 16, None) == _lib.AFA_ERR_INVALID
+    assert b"afa_ring_pull" in lib.afa_last_error()
+    assert lib.afa_ring_pull(None, None, 0, None) == _lib.AFA_OK

@@ -13,7 +13,7 @@ import torch
 
 import algebraic_intelligence_b200 as afa
 from algebraic_intelligence_b200.afa import hop_forward
-from algebraic_intelligence_b200.ring import ring_loop, ring_plan, shard_sequence, unshard_sequence
+from algebraic_intelligence_b200.ring import ListExchange, ring_loop, ring_plan, shard_sequence, unshard_sequence
 from algebraic_intelligence_b200 import _lib
 import inputs
 from oracle import afa_oracle as orc
@@ -106,11 +106,6 @@ def test_decode_matches_prefill_row():
 # ---------------------------------------------------------------------------
 # ring, emulated on one GPU
 # ---------------------------------------------------------------------------
-class _Done:
-    def wait(self):
-        pass
-
-
 def emulate_ring(q, k, v, world, causal, layout, sink=0.5):
     """Runs ring_plan + ring_loop + the hop kernel for every rank on this GPU."""
     seq = q.shape[2]
@@ -126,17 +121,11 @@ def emulate_ring(q, k, v, world, causal, layout, sink=0.5):
         out = torch.full_like(qs, float("nan"))
         den = torch.empty((b, h, s, 1), dtype=acc, device=q.device)
         hops = ring_plan(r, world, seq, causal, layout)
-        later = iter([kvs[(r - i) % world] for i in range(1, world)])
-
-        def rotate(send, recv):
-            recv.copy_(next(later))
-            return [_Done()]
-
         def compute(hop, kk, vv):
             hop_forward(qs, kk, vv, hop.problems, causal, hop.mode, o_acc=o_acc, d_acc=d_acc, out=out,
                         d_total=den, sink_omega=sink)
 
-        ring_loop(qs, kvs[r].clone(), hops, compute, rotate if world > 1 else None)
+        ring_loop(kvs[r][0], kvs[r][1], hops, compute, ListExchange(r, kvs) if world > 1 else None)
         outs.append(out)
     return unshard_sequence(outs, layout)
 

@@ -1,9 +1,12 @@
-"""Ring AFA across real GPUs: one process per GPU, K/V rotated with NCCL
-send/recv (skipped unless at least two GPUs are visible).
+"""Ring AFA across real GPUs: one process per GPU, each hop's K/V pulled from
+its owner through CUDA IPC and the copy engines, one NCCL barrier per call
+(skipped unless at least two GPUs are visible).
 
 Each rank checks its output shard against the single-GPU forward of the full
 sequence computed on its own GPU: float32 <= 1e-6 relative (the north-star ring
-bound), bf16 against the oracle at 2e-2.
+bound), bf16 at 1e-2. Every worker makes three ring calls in a row with
+different inputs, so the alternating published buffers and the cached exchange
+are both exercised.
 """
 import os
 import socket
@@ -39,14 +42,16 @@ def _worker(rank, world, port, dtype_name, layout, causal, results):
         dtype = getattr(torch, dtype_name)
         g = torch.Generator(device="cuda").manual_seed(11)
         shape = (1, 4, 1024 * world, 128)
-        q, k, v = (torch.randn(shape, generator=g, device="cuda").to(dtype) for _ in range(3))
-        qs, ks, vs = (shard_sequence(t, rank, world, layout) for t in (q, k, v))
-        y = afa.distributed_ring_afa(qs, ks, vs, causal=causal, num_devices=world, layout=layout)
-        single = shard_sequence(afa.pallas_afa_forward(q, k, v, causal=causal), rank, world, layout)
-        a = y.to(torch.float64).cpu().numpy()
-        b = single.to(torch.float64).cpu().numpy()
-        err = float(np.max(np.abs(a - b)) / np.max(np.abs(b)))
-        results[rank] = err
+        errs = []
+        for _call in range(3):
+            q, k, v = (torch.randn(shape, generator=g, device="cuda").to(dtype) for _ in range(3))
+            qs, ks, vs = (shard_sequence(t, rank, world, layout) for t in (q, k, v))
+            y = afa.distributed_ring_afa(qs, ks, vs, causal=causal, num_devices=world, layout=layout)
+            single = shard_sequence(afa.pallas_afa_forward(q, k, v, causal=causal), rank, world, layout)
+            a = y.to(torch.float64).cpu().numpy()
+            b = single.to(torch.float64).cpu().numpy()
+            errs.append(float(np.max(np.abs(a - b)) / np.max(np.abs(b))))
+        results[rank] = max(errs)
     finally:
         dist.destroy_process_group()
 
@@ -71,3 +76,73 @@ def test_nccl_ring_matches_single_gpu(dtype_name, tol, layout):
         p.join(300)
     assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
     assert max(results.values()) <= tol, dict(results)
+
+
+def _pull_worker(rank, world, port, results):
+    """Every rank publishes a buffer filled with its rank and pulls every
+    peer's through the C ABI (afa_ring_export / afa_ring_open / afa_ring_pull)."""
+    import ctypes
+    import datetime
+
+    import torch.distributed as dist
+
+    from algebraic_intelligence_b200 import _lib
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    try:
+        lib = _lib.load()
+        # An odd offset into a larger allocation: the exported handle covers the
+        # allocation, the offset locates the buffer in it.
+        backing = torch.zeros(3 << 20, dtype=torch.int32, device="cuda")
+        pub = backing[4096 + 7:4096 + 7 + (1 << 20)]
+        pub.fill_(rank + 1)
+        handle = (ctypes.c_ubyte * 64)()
+        off = ctypes.c_ulonglong(0)
+        _lib.check(lib.afa_ring_export(pub.data_ptr(), handle, ctypes.byref(off)), "export")
+        mine = torch.tensor(list(bytes(handle)) + list(off.value.to_bytes(8, "little")), dtype=torch.uint8,
+                            device="cuda")
+        every = [torch.empty_like(mine) for _ in range(world)]
+        dist.all_gather(every, mine)
+        torch.cuda.synchronize()
+        dist.barrier()
+        ok = True
+        dst = torch.empty_like(pub)
+        for j in range(world):
+            if j == rank:
+                continue
+            raw = bytes(every[j].cpu().tolist())
+            base = ctypes.c_void_p()
+            _lib.check(lib.afa_ring_open(raw[:64], ctypes.byref(base)), "open")
+            src = base.value + int.from_bytes(raw[64:72], "little")
+            dst.zero_()
+            _lib.check(lib.afa_ring_pull(dst.data_ptr(), src, pub.numel() * 4, _lib.stream_ptr(dst.device)),
+                       "pull")
+            torch.cuda.synchronize()
+            ok = ok and bool((dst == j + 1).all())
+            _lib.check(lib.afa_ring_close(base.value), "close")
+        dist.barrier()
+        results[rank] = ok
+    finally:
+        dist.destroy_process_group()
+
+
+def test_ring_exchange_pulls_every_peer():
+    n = torch.cuda.device_count()
+    if n < 2:
+        pytest.skip("needs at least two GPUs")
+    world = min(n, 8)
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    results = ctx.Manager().dict()
+    port = _free_port()
+    procs = [ctx.Process(target=_pull_worker, args=(r, world, port, results)) for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(300)
+    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+    assert all(results[r] for r in range(world)), dict(results)

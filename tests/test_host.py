@@ -1,6 +1,6 @@
 """Host-side logic without a GPU: argument checks with the reference's exception
 types and messages, and the ring plan (zigzag / contiguous sharding, hop modes,
-K/V rotation over gloo)."""
+the ring's K/V exchange protocol over gloo)."""
 import os
 
 import numpy as np
@@ -9,7 +9,8 @@ import torch
 
 import algebraic_intelligence_b200 as afa
 from algebraic_intelligence_b200 import _lib
-from algebraic_intelligence_b200.ring import local_segments, ring_loop, ring_plan, shard_sequence, unshard_sequence
+from algebraic_intelligence_b200.ring import (KVExchange, ListExchange, local_segments, ring_loop, ring_plan,
+                                              shard_sequence, unshard_sequence)
 from oracle import afa_oracle as orc
 
 
@@ -92,7 +93,7 @@ def test_shard_roundtrip(world, layout):
 
 def _simulate_ring(q, k, v, world, causal, layout, sink=0.5):
     """Runs ring_plan + ring_loop for every rank in-process; the hop compute is
-    the oracle (the checker), the rotation a list shift."""
+    the oracle (the checker), the exchange a list of every rank's shard."""
     seq = q.shape[2]
     qs = [shard_sequence(q, r, world, layout) for r in range(world)]
     kvs = [torch.stack([shard_sequence(k, r, world, layout), shard_sequence(v, r, world, layout)])
@@ -104,15 +105,6 @@ def _simulate_ring(q, k, v, world, causal, layout, sink=0.5):
         o_acc = np.zeros(qs[r].shape)
         d_acc = np.zeros(qs[r].shape[:3])
         out = np.full(qs[r].shape, np.nan)
-        class _Req:
-            def wait(self):
-                pass
-
-        def rotate(send, recv):
-            recv.copy_(next(visits_after))
-            return [_Req()]
-
-        visits_after = iter([kvs[(r - h) % world] for h in range(1, world)])
 
         def compute(hop, kk, vv):
             assert torch.equal(torch.stack([kk, vv]), kvs[hop.src])
@@ -136,7 +128,8 @@ def _simulate_ring(q, k, v, world, causal, layout, sink=0.5):
                 else:
                     out[:, :, sl] = num / (rs + sink)
 
-        ring_loop(qs[r], kvs[r].clone(), hops, compute, rotate if world > 1 else None)
+        ex = ListExchange(r, kvs) if world > 1 else None
+        ring_loop(kvs[r][0], kvs[r][1], hops, compute, ex)
         assert s == qs[r].shape[2]
         outs.append(torch.from_numpy(out))
     return unshard_sequence(outs, layout).numpy()
@@ -181,45 +174,94 @@ def test_first_hop_covers_every_query_segment():
                     assert last == covered  # every row gets its final divide
 
 
-def _gloo_worker(rank, world, port, results):
+class _SharedMemoryExchange(KVExchange):
+    """The CUDA IPC exchange's protocol on CPU processes: published buffers are
+    shared-memory tensors every process maps, the barriers gloo barriers, a
+    pull a copy out of the owner's buffer. ``pubs[r]`` is rank r's."""
+
+    def __init__(self, rank, pubs, log):
+        import torch.distributed as dist
+        self.dist = dist
+        self.rank = rank
+        self.pubs = pubs
+        self.recv = [torch.empty_like(pubs[rank]) for _ in range(2)]
+        self.log = log
+
+    def publish(self, k, v):
+        buf = self.pubs[self.rank]
+        buf[0].copy_(k)
+        buf[1].copy_(v)
+        self.dist.barrier()
+        return buf
+
+    def pull(self, src, slot):
+        self.log.append(("pull", src, slot))
+        self.recv[slot].copy_(self.pubs[src])
+        return slot
+
+    def ready(self, token):
+        return self.recv[token]
+
+    def finish(self):
+        self.log.append(("end",))
+        self.dist.barrier()
+
+
+def _gloo_worker(rank, world, port, pubs, causal, results):
     import torch.distributed as dist
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
-        from algebraic_intelligence_b200.ring import _p2p_rotate
-        kv = torch.full((2, 1, 1, 4, 2), float(rank))
-        seen = [kv.clone()]
-        hops = ring_plan(rank, world, 4 * world, False, "contiguous")
+        log = []
+        ex = _SharedMemoryExchange(rank, pubs, log)
+        hops = ring_plan(rank, world, 4 * world, causal, "contiguous")
+        seen = []
+        for call in range(3):
+            # K carries (call, rank) so a hop that read a stale or foreign buffer shows it.
+            k = torch.full((1, 1, 4, 2), float(100 * call + rank))
+            v = -k
 
-        def compute(hop, kk, vv):
-            seen.append(torch.stack([kk, vv]).clone())
+            def compute(hop, kk, vv):
+                assert torch.equal(vv, -kk)
+                seen.append((call, hop.src, int(kk[0, 0, 0, 0])))
 
-        ring_loop(torch.zeros(1, 1, 4, 2), kv, hops, compute,
-                  lambda s, r: _p2p_rotate(s, r, rank, world, None))
-        results[rank] = [int(t[0, 0, 0, 0, 0]) for t in seen[1:]]
+            # No barrier between calls besides the exchange's own: they alone
+            # must keep a fast rank from overwriting what a slow rank still reads.
+            ring_loop(k, v, hops, compute, ex)
+        results[rank] = (seen, log)
     finally:
         dist.destroy_process_group()
 
 
 @pytest.mark.parametrize("world", [2, 3])
-def test_ring_rotation_over_gloo(world):
-    """Each rank sees the K/V shards of ranks r, r-1, r-2, ... in hop order
-    (the ppermute direction of pallas_afa.py:632, :651-652)."""
+@pytest.mark.parametrize("causal", [False, True])
+def test_ring_exchange_protocol_over_gloo(world, causal):
+    """Real processes run the ring's publish / barrier / pull protocol over
+    shared memory: every hop reads the shard of rank r-h of the same call (the
+    ppermute order of pallas_afa.py:632, :651-652), wholly masked hops pull
+    nothing, and every call ends with its barrier."""
     import socket
 
     import torch.multiprocessing as mp
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
         port = s.getsockname()[1]
+    pubs = [torch.zeros(2, 1, 1, 4, 2).share_memory_() for _ in range(world)]
     ctx = mp.get_context("spawn")
     mgr = ctx.Manager()
     results = mgr.dict()
-    procs = [ctx.Process(target=_gloo_worker, args=(r, world, port, results)) for r in range(world)]
+    procs = [ctx.Process(target=_gloo_worker, args=(r, world, port, pubs, causal, results)) for r in range(world)]
     for p in procs:
         p.start()
     for p in procs:
         p.join(120)
         assert p.exitcode == 0
     for r in range(world):
-        assert results[r] == [(r - h) % world for h in range(world)]
+        seen, log = results[r]
+        hops = ring_plan(r, world, 4 * world, causal, "contiguous")
+        want_src = [h.src for h in hops if h.problems]
+        want = [(c, s, 100 * c + s) for c in range(3) for s in want_src]
+        assert seen == want
+        pulls = [(h.src, i % 2) for i, h in enumerate(hops) if i > 0 and h.problems]
+        assert log == [e for _ in range(3) for e in [("pull", s, slot) for s, slot in pulls] + [("end",)]]
