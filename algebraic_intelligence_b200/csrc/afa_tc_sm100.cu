@@ -37,6 +37,8 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
+#include <algorithm>
+
 #include "afa_common.cuh"
 #include "afa_internal.h"
 
@@ -73,7 +75,7 @@ struct TcCfg {
 
 // Key tiles of one segment visible from a query tile whose last valid row sits
 // at global position qpos_last.
-__device__ __forceinline__ int seg_tiles(const Segment& ks, int causal, int qpos_last) {
+__host__ __device__ __forceinline__ int seg_tiles(const Segment& ks, int causal, int qpos_last) {
   int n = ks.len;
   if (causal) {
     const int m = qpos_last - ks.pos0 + 1;
@@ -88,7 +90,7 @@ struct KvTile {
   int lim;  // valid keys in the tile (1..128)
 };
 
-__device__ __forceinline__ KvTile kv_tile(const Problem& P, int cnt_seg0, int t) {
+__host__ __device__ __forceinline__ KvTile kv_tile(const Problem& P, int cnt_seg0, int t) {
   const int s = (t < cnt_seg0) ? 0 : 1;
   const int jj = s ? t - cnt_seg0 : t;
   const Segment& ks = P.k[s];
@@ -98,6 +100,40 @@ __device__ __forceinline__ KvTile kv_tile(const Problem& P, int cnt_seg0, int t)
   const int lim = ks.len - jj * 128;
   kt.lim = lim < 128 ? lim : 128;
   return kt;
+}
+
+// Geometry of query pair `cta` (two 128-row query tiles) of a launch: its
+// problem, first row, and key-tile counts. Only the last key segment may be
+// partially visible, which makes tile 0's key tiles a prefix of tile 1's.
+struct PairGeom {
+  int pi;      // problem index
+  int r0;      // first row of query tile 0 in the problem's q segment
+  int n0, n1;  // key tiles of query tile 0 / 1
+  int cnt1_0;  // tile 1's key tiles in key segment 0
+};
+
+__host__ __device__ __forceinline__ PairGeom pair_geom(const Launch& L, int cta) {
+  PairGeom G;
+  int pi = 0;
+  for (int i = 1; i < kMaxProblems; ++i)
+    if (i < L.nprob && cta >= L.prob[i].cta0) pi = i;
+  const Problem& P = L.prob[pi];
+  G.pi = pi;
+  G.r0 = (cta - P.cta0) * 256;
+  const bool q1_live = G.r0 + 128 < P.q.len;
+  const int last0 = (G.r0 + 127 < P.q.len - 1) ? G.r0 + 127 : P.q.len - 1;
+  const int last1 = q1_live ? ((G.r0 + 255 < P.q.len - 1) ? G.r0 + 255 : P.q.len - 1) : last0;
+  int cnt0[2] = {0, 0}, cnt1[2] = {0, 0};
+  for (int s = 0; s < kMaxKSegs; ++s) {
+    if (s < P.nk) {
+      cnt0[s] = seg_tiles(P.k[s], L.causal, P.q.pos0 + last0);
+      cnt1[s] = seg_tiles(P.k[s], L.causal, P.q.pos0 + last1);
+    }
+  }
+  G.n1 = cnt1[0] + cnt1[1];
+  G.n0 = (P.nk == 1 || cnt0[0] == cnt1[0]) ? cnt0[0] + cnt0[1] : G.n1;
+  G.cnt1_0 = cnt1[0];
+  return G;
 }
 
 // Octic map of one 32-column chunk of a score row, written back as 16 packed
@@ -434,6 +470,405 @@ __global__ void __launch_bounds__(576, 1)
   }
 }
 
+// ---------------------------------------------------------------------------
+// Persistent stream-K kernel for the accumulate hop modes.
+//
+// A ring hop whose query pairs all see the same number of key tiles launches
+// equal CTAs, and 256 or 512 of them on 148 SMs leave the last wave partly
+// empty (about 13% of the hop); each CTA also ends with a read-modify-write of
+// its fp32 accumulator rows. Accumulate-mode launches therefore run one CTA per
+// SM (G CTAs) over a hybrid schedule. The (b, h, query pair) items are
+// numbered with b*h varying fastest, as in the non-persistent grid. Whole
+// rounds of items come first: CTA c takes items c, c+G, c+2G, ..., so the CTAs
+// of a round sweep the same heads' keys together and share K/V tiles in L2.
+// The key-tile iterations of the remaining items (less than one round) are
+// then split evenly: CTA c takes the c-th of G equal contiguous ranges, and an
+// item whose iterations straddle two ranges is computed in two pieces. AFA
+// partial results only add (there is no running maximum to reconcile), so
+// every piece adds its numerator and row sums into the fp32 accumulators with
+// red.global.add: fire-and-forget reductions with no ordering between pieces.
+// In kAccumFinal the divide runs afterwards over the problems' rows
+// (sk_finalize_kernel). There is no named barrier and no inter-CTA wait; every
+// wait is a bounded mbarrier wait as in afa_tc_fwd_kernel.
+constexpr int kMaxSkItems = 1024;
+
+struct SkPlan {
+  int nitems;                   // listed query pairs per (b, h)
+  int nbh;                      // B * H
+  int waves;                    // rounds of whole items
+  int prefix[kMaxSkItems + 1];  // key-tile iterations before listed pair i; prefix[nitems] = per (b, h)
+  int pair_of[kMaxSkItems];     // launch pair (pair_geom index) of listed pair i
+};
+
+struct SkSeg {
+  int bh, item, t0, t1;  // key tiles [t0, t1) of listed pair `item` of head bh
+};
+
+// Iterations of linear items [0, j) (item j = pair j / nbh of head j % nbh).
+__host__ __device__ __forceinline__ long long sk_before(const SkPlan& S, long long j) {
+  const int pair = static_cast<int>(j / S.nbh);
+  const int hh = static_cast<int>(j - static_cast<long long>(pair) * S.nbh);
+  const long long base = static_cast<long long>(S.nbh) * S.prefix[pair];
+  return pair >= S.nitems ? base : base + static_cast<long long>(hh) * (S.prefix[pair + 1] - S.prefix[pair]);
+}
+
+// The pieces CTA c of G computes, in order; every role of the CTA walks the
+// same sequence.
+struct SkWalk {
+  const SkPlan* S;
+  int G, c, k;
+  long long j0, total, i, hi;
+
+  __device__ __forceinline__ void init(const SkPlan& s, int G_, int c_) {
+    S = &s;
+    G = G_;
+    c = c_;
+    k = 0;
+    total = static_cast<long long>(s.nbh) * s.nitems;
+    j0 = static_cast<long long>(s.waves) * G;
+    const long long i0 = sk_before(s, j0);
+    const long long tail = sk_before(s, total) - i0;
+    i = i0 + tail * c / G;
+    hi = i0 + tail * (c + 1) / G;
+  }
+
+  __device__ __forceinline__ bool next(SkSeg& sg) {
+    while (k < S->waves) {  // whole items
+      const long long j = static_cast<long long>(k++) * G + c;
+      const int item = static_cast<int>(j / S->nbh);
+      const int n = S->prefix[item + 1] - S->prefix[item];
+      if (n > 0) {
+        sg.bh = static_cast<int>(j - static_cast<long long>(item) * S->nbh);
+        sg.item = item;
+        sg.t0 = 0;
+        sg.t1 = n;
+        return true;
+      }
+    }
+    if (i >= hi) return false;  // split tail: the item holding iteration i
+    long long lo = j0, up = total;  // sk_before(lo) <= i < sk_before(up)
+    while (up - lo > 1) {
+      const long long mid = (lo + up) >> 1;
+      if (sk_before(*S, mid) <= i) lo = mid; else up = mid;
+    }
+    const int item = static_cast<int>(lo / S->nbh);
+    sg.bh = static_cast<int>(lo - static_cast<long long>(item) * S->nbh);
+    sg.item = item;
+    sg.t0 = static_cast<int>(i - sk_before(*S, lo));
+    const int n = S->prefix[item + 1] - S->prefix[item];
+    const long long rem = hi - i;
+    sg.t1 = rem < static_cast<long long>(n - sg.t0) ? sg.t0 + static_cast<int>(rem) : n;
+    i += sg.t1 - sg.t0;
+    return true;
+  }
+};
+
+__device__ __forceinline__ void red_add_v4(float* p, float a, float b, float c, float d) {
+  asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(p), "f"(a), "f"(b), "f"(c), "f"(d) : "memory");
+}
+
+__device__ __forceinline__ void red_add(float* p, float a) {
+  asm volatile("red.global.add.f32 [%0], %1;" ::"l"(p), "f"(a) : "memory");
+}
+
+template <int HD>
+__global__ void __launch_bounds__(576, 1)
+    afa_tc_sk_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                     const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ Launch L,
+                     const __grid_constant__ SkPlan S) {
+  using C = TcCfg<HD>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::BAR_OFF);
+  uint64_t* q_full = bars;
+  uint64_t* kv_full = bars + 1;
+  uint64_t* kv_empty = kv_full + C::NSLOT;
+  uint64_t* s_full = kv_empty + C::NSLOT;
+  uint64_t* p_full = s_full + 2;
+  uint64_t* o_full = p_full + 2;
+  uint64_t* drain = o_full + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  uint64_t* q_empty = reinterpret_cast<uint64_t*>(smem + C::RED_OFF);  // the row-sum exchange area is unused here
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  SkWalk walk;
+  walk.init(S, gridDim.x, blockIdx.x);
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    mbar_init(q_empty, 1);
+    for (int s = 0; s < C::NSLOT; ++s) {
+      mbar_init(kv_full + s, 1);
+      mbar_init(kv_empty + s, 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(s_full + i, 1);
+      mbar_init(p_full + i, 16);
+      mbar_init(o_full + i, 1);
+    }
+    mbar_init(drain, 1);
+    fence_barrier_init();
+    fence_proxy_async_smem();
+    prefetch_tmap(&tm_q);
+    prefetch_tmap(&tm_k);
+    prefetch_tmap(&tm_v);
+  }
+  if (warp == C::kMmaWarp) {
+    tmem_alloc(tmem_slot, C::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == C::kTmaWarp) {
+    // ------------------------------------------------------------------ TMA
+    if (lane == 0) {
+      SkSeg sg;
+      int u = 0, qn = 0;
+      bool ok = true;
+      while (ok && walk.next(sg)) {
+        const PairGeom G = pair_geom(L, S.pair_of[sg.item]);
+        const Problem& P = L.prob[G.pi];
+        // The previous piece's last S = Q K^T must be done with the Q tiles.
+        if (qn > 0 && !(ok = mbar_wait(q_empty, (qn - 1) & 1, L.status, kDevTimeoutProducer))) break;
+        mbar_arrive_expect_tx(q_full, 2 * C::TILE_BYTES);
+        for (int q = 0; q < 2; ++q)
+          for (int h = 0; h < C::KSUB; ++h)
+            tma_load_3d(smem + C::Q_OFF + (q * C::KSUB + h) * C::SUB_BYTES, &tm_q, q_full, 64 * h,
+                        P.q.row0 + G.r0 + 128 * q, sg.bh);
+        ++qn;
+        for (int t = sg.t0; ok && t < sg.t1; ++t) {
+          const KvTile kt = kv_tile(P, G.cnt1_0, t);
+          for (int kv = 0; kv < 2; ++kv) {
+            const int slot = u % C::NSLOT;
+            if (!(ok = mbar_wait(kv_empty + slot, ((u / C::NSLOT) & 1) ^ 1, L.status, kDevTimeoutProducer))) break;
+            mbar_arrive_expect_tx(kv_full + slot, C::TILE_BYTES);
+            for (int h = 0; h < C::KSUB; ++h)
+              tma_load_3d(smem + C::KV_OFF + (slot * C::KSUB + h) * C::SUB_BYTES, kv ? &tm_v : &tm_k,
+                          kv_full + slot, 64 * h, kt.row, sg.bh);
+            ++u;
+          }
+        }
+      }
+      // Do not leave the CTA while loads into its shared memory are in flight.
+      if (qn > 0) (void)mbar_wait(q_full, (qn - 1) & 1, nullptr, 0);
+      for (int x = u - C::NSLOT < 0 ? 0 : u - C::NSLOT; x < u; ++x)
+        (void)mbar_wait(kv_full + (x % C::NSLOT), (x / C::NSLOT) & 1, nullptr, 0);
+    }
+  } else if (warp == C::kMmaWarp) {
+    // ------------------------------------------------------------------ MMA
+    if (lane == 0) {
+      constexpr uint32_t idesc_s = idesc_bf16_f32(128, 128, false);
+      constexpr uint32_t idesc_o = idesc_bf16_f32(128, HD, true);
+      const uint32_t q_base = smem_u32(smem + C::Q_OFF);
+      const uint32_t kv_base = smem_u32(smem + C::KV_OFF);
+      auto issue_s = [&](int q, int slot) {
+#pragma unroll
+        for (int kk = 0; kk < HD / 16; ++kk) {
+          const uint32_t off = (kk & 3) * 32;
+          const uint64_t a = sw128_desc(q_base + (q * C::KSUB + (kk >> 2)) * C::SUB_BYTES + off, 16, 1024);
+          const uint64_t b = sw128_desc(kv_base + (slot * C::KSUB + (kk >> 2)) * C::SUB_BYTES + off, 16, 1024);
+          umma_ss(tmem + C::s_col(q), a, b, idesc_s, kk > 0 ? 1u : 0u);
+        }
+      };
+      auto issue_o = [&](int q, int slot, bool acc) {
+#pragma unroll
+        for (int kk = 0; kk < C::BN / 16; ++kk) {
+          const uint64_t b = sw128_desc(kv_base + slot * C::TILE_BYTES + kk * 2048, C::SUB_BYTES, 1024);
+          umma_ts(tmem + C::o_col(q), tmem + C::s_col(q) + C::p_col(kk), b, idesc_o, (acc || kk > 0) ? 1u : 0u);
+        }
+      };
+      SkSeg sg;
+      int qn = 0, ub = 0, pc[2] = {0, 0};
+      bool ok = true;
+      while (ok && walk.next(sg)) {
+        const PairGeom G = pair_geom(L, S.pair_of[sg.item]);
+        const int t0 = sg.t0, t1 = sg.t1;
+        const int e0 = t1 < G.n0 ? t1 : G.n0;  // query tile 0 is live for t in [t0, e0)
+        const int sk0 = ub % C::NSLOT;
+        if (!(ok = mbar_wait(q_full, qn & 1, L.status, kDevTimeoutMma) &&
+                   mbar_wait(kv_full + sk0, (ub / C::NSLOT) & 1, L.status, kDevTimeoutMma)))
+          break;
+        ++qn;
+        tc_fence_after();
+        // The previous piece's O reads finished before its P arrivals of this
+        // piece (the octic warps run the epilogue first), so the first P.V
+        // below may overwrite O; S regions are free once the previous P.V ran,
+        // which the in-order tensor pipe guarantees.
+        if (t0 < e0) {
+          issue_s(0, sk0);
+          umma_commit(s_full + 0);
+        }
+        issue_s(1, sk0);
+        umma_commit(s_full + 1);
+        umma_commit(kv_empty + sk0);
+        if (t1 - t0 == 1) umma_commit(q_empty);
+        for (int t = t0; ok && t < t1; ++t) {
+          const int uv = ub + 2 * (t - t0) + 1, sv = uv % C::NSLOT;
+          const int uk = uv + 1, sk = uk % C::NSLOT;
+          const bool more = t + 1 < t1;
+          if (!(ok = mbar_wait(kv_full + sv, (uv / C::NSLOT) & 1, L.status, kDevTimeoutMma))) break;
+          if (more && !(ok = mbar_wait(kv_full + sk, (uk / C::NSLOT) & 1, L.status, kDevTimeoutMma))) break;
+          if (t < e0) {
+            if (!(ok = mbar_wait(p_full + 0, pc[0] & 1, L.status, kDevTimeoutMma))) break;
+            ++pc[0];
+            tc_fence_after();
+            issue_o(0, sv, t > t0);
+            if (t + 1 == e0) umma_commit(o_full + 0);
+            if (more && t + 1 < e0) {
+              issue_s(0, sk);
+              umma_commit(s_full + 0);
+            }
+          }
+          if (!(ok = mbar_wait(p_full + 1, pc[1] & 1, L.status, kDevTimeoutMma))) break;
+          ++pc[1];
+          tc_fence_after();
+          issue_o(1, sv, t > t0);
+          umma_commit(kv_empty + sv);
+          if (t + 1 == t1) umma_commit(o_full + 1);
+          if (more) {
+            issue_s(1, sk);
+            umma_commit(s_full + 1);
+            umma_commit(kv_empty + sk);
+            if (t + 2 == t1) umma_commit(q_empty);
+          }
+        }
+        ub += 2 * (t1 - t0);
+      }
+      // Every MMA this thread issued must finish before TMEM is released.
+      umma_commit(drain);
+      (void)mbar_wait(drain, 0, nullptr, 0);
+    }
+  } else {
+    // ------------------------------------- octic map + accumulate epilogue
+    const int g = warp >> 2;
+    const int sub = warp & 3;
+    const int row = sub * 32 + lane;
+    const uint32_t lane_off = static_cast<uint32_t>(sub * 32) << 16;
+    const float scale = L.scale;
+    constexpr int OC = HD / 4;
+    SkSeg sg;
+    int sc[2] = {0, 0}, oc[2] = {0, 0};
+    bool ok = true;
+    while (ok && walk.next(sg)) {
+      const PairGeom G = pair_geom(L, S.pair_of[sg.item]);
+      const Problem& P = L.prob[G.pi];
+      const int e0 = sg.t1 < G.n0 ? sg.t1 : G.n0;
+      float dsum[2] = {0.f, 0.f};
+      for (int t = sg.t0; t < sg.t1 && ok; ++t) {
+        const KvTile kt = kv_tile(P, G.cnt1_0, t);
+#pragma unroll
+        for (int tile = 0; tile < 2; ++tile) {
+          if (tile == 0 && t >= e0) continue;
+          ok = mbar_wait(s_full + tile, sc[tile] & 1, L.status, kDevTimeoutSoftmax);
+          ++sc[tile];
+          ok = __all_sync(0xffffffffu, ok);
+          if (!ok) break;
+          tc_fence_after();
+          const int qfirst = P.q.pos0 + G.r0 + 128 * tile;
+          const int qpos = qfirst + row;
+          const bool need_mask = kt.lim < 128 || (L.causal && kt.pos + 127 > qfirst);
+          const uint32_t s_tm = tmem + C::s_col(tile) + lane_off + 32 * g;
+          uint32_t sv[32];
+          uint32_t pk[16];
+          tmem_ld32(s_tm, sv);
+          tmem_ld_wait();
+          const float part = need_mask ? map_chunk<true>(sv, pk, scale, 32 * g, kt.lim, L.causal, kt.pos, qpos)
+                                       : map_chunk<false>(sv, pk, scale, 32 * g, kt.lim, L.causal, kt.pos, qpos);
+          tmem_st16(s_tm, pk);
+          tmem_st_wait();
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(p_full + tile);
+          dsum[tile] += part;
+        }
+      }
+      // Add this piece into the accumulators. Every warpgroup adds its own
+      // columns of O and its own partial row sum (four adds per row).
+#pragma unroll
+      for (int tile = 0; tile < 2; ++tile) {
+        if (tile == 0 && sg.t0 >= e0) continue;  // tile 0 had no key tiles in this piece
+        if (!ok) break;
+        ok = mbar_wait(o_full + tile, oc[tile] & 1, L.status, kDevTimeoutEpilogue);
+        ++oc[tile];
+        ok = __all_sync(0xffffffffu, ok);
+        if (!ok) break;
+        tc_fence_after();
+        const int rloc = G.r0 + 128 * tile + row;
+        const long long grow = static_cast<long long>(sg.bh) * L.lq + P.q.row0 + rloc;
+        uint32_t ov[32];
+        __syncwarp();  // tcgen05.ld is warp-collective
+        const uint32_t o_tm = tmem + C::o_col(tile) + lane_off + OC * g;
+        if constexpr (OC == 32) {
+          tmem_ld32(o_tm, ov);
+        } else {
+          uint32_t (&ov16)[16] = *reinterpret_cast<uint32_t(*)[16]>(ov);
+          tmem_ld16(o_tm, ov16);
+        }
+        tmem_ld_wait();
+        if (rloc < P.q.len) {
+          float* acc_row = static_cast<float*>(L.o_acc) + grow * HD + OC * g;
+#pragma unroll
+          for (int w = 0; w < OC / 4; ++w)
+            red_add_v4(acc_row + 4 * w, __uint_as_float(ov[4 * w + 0]), __uint_as_float(ov[4 * w + 1]),
+                       __uint_as_float(ov[4 * w + 2]), __uint_as_float(ov[4 * w + 3]));
+          red_add(static_cast<float*>(L.d_acc) + grow, dsum[tile]);
+        }
+      }
+      // The O reads above are complete (wait::ld) before this warp's next
+      // P arrival, which is what lets the MMA warp overwrite O.
+      tc_fence_before();
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == C::kMmaWarp) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem, C::TMEM_COLS);
+  }
+}
+
+// out = o_acc / (d_acc + sink) and d_total = d_acc + sink over the rows of the
+// launch's problems: the divide of kAccumFinal after afa_tc_sk_kernel added the
+// last hop in (pallas_afa.py:661). One warp per row.
+template <int HD>
+__global__ void __launch_bounds__(256) sk_finalize_kernel(const __grid_constant__ Launch L) {
+  constexpr int VPL = HD / 32;  // fp32 columns per lane: 4 or 2
+  int rows_bh = 0;
+  for (int p = 0; p < L.nprob; ++p) rows_bh += L.prob[p].q.len;
+  const long long total = static_cast<long long>(L.B) * L.H * rows_bh;
+  const int lane = threadIdx.x & 31;
+  for (long long r = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5; r < total;
+       r += (static_cast<long long>(gridDim.x) * blockDim.x) >> 5) {
+    const int bh = static_cast<int>(r / rows_bh);
+    int w = static_cast<int>(r - static_cast<long long>(bh) * rows_bh);
+    int p = 0;
+    while (w >= L.prob[p].q.len) w -= L.prob[p++].q.len;
+    const long long grow = static_cast<long long>(bh) * L.lq + L.prob[p].q.row0 + w;
+    const float d = static_cast<const float*>(L.d_acc)[grow];
+    const float denom = d + L.sink;
+    const float inv = 1.0f / denom;
+    const float* src = static_cast<const float*>(L.o_acc) + grow * HD + VPL * lane;
+    __nv_bfloat16* dst = static_cast<__nv_bfloat16*>(L.out) + grow * HD + VPL * lane;
+    if constexpr (VPL == 4) {
+      const float4 x = *reinterpret_cast<const float4*>(src);
+      uint2 pkt;
+      pkt.x = pack_bf16x2(x.x * inv, x.y * inv);
+      pkt.y = pack_bf16x2(x.z * inv, x.w * inv);
+      *reinterpret_cast<uint2*>(dst) = pkt;
+    } else {
+      const float2 x = *reinterpret_cast<const float2*>(src);
+      *reinterpret_cast<uint32_t*>(dst) = pack_bf16x2(x.x * inv, x.y * inv);
+    }
+    if (lane == 0 && L.dtot) static_cast<float*>(L.dtot)[grow] = denom;
+  }
+}
+
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
   static bool tried = false;
@@ -469,9 +904,13 @@ cudaError_t launch_hd(const Launch& L, cudaStream_t stream, const char** detail)
   static bool attr_set[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
+  static int sm_count[64] = {};
   if (dev < 64 && !attr_set[dev]) {
     cudaError_t e = cudaFuncSetAttribute(afa_tc_fwd_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          C::SMEM_BYTES);
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(afa_tc_sk_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
+    if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sm_count[dev], cudaDevAttrMultiProcessorCount, dev);
     if (e != cudaSuccess) {
       *detail = "cudaFuncSetAttribute(max dynamic shared memory) failed";
       return e;
@@ -488,6 +927,42 @@ cudaError_t launch_hd(const Launch& L, cudaStream_t stream, const char** detail)
   Launch LL = L;
   const int total = assign_ctas(LL, 256);
   if (total == 0) return cudaSuccess;
+  if ((LL.mode == kAccumRaw || LL.mode == kAccumFinal) && total <= kMaxSkItems && dev < 64) {
+    // Accumulate modes: persistent stream-K over equal shares of the key-tile
+    // iterations, pieces added with reductions; then the divide for kAccumFinal.
+    // The pairs with key tiles, longest first (stable): whole-item rounds then
+    // hold items of similar length.
+    SkPlan S;
+    int len[kMaxSkItems];
+    S.nitems = 0;
+    for (int c = 0; c < total; ++c) {
+      len[c] = pair_geom(LL, c).n1;
+      if (len[c] > 0) S.pair_of[S.nitems++] = c;
+    }
+    std::stable_sort(S.pair_of, S.pair_of + S.nitems, [&](int a, int b) { return len[a] > len[b]; });
+    S.nbh = bh;
+    S.prefix[0] = 0;
+    for (int i = 0; i < S.nitems; ++i) S.prefix[i + 1] = S.prefix[i] + len[S.pair_of[i]];
+    const long long W = static_cast<long long>(bh) * S.prefix[S.nitems];
+    if (W > 0) {
+      long long G = W / 8;  // at least 8 key tiles per CTA
+      if (G > sm_count[dev]) G = sm_count[dev];
+      if (G < 1) G = 1;
+      S.waves = static_cast<int>(static_cast<long long>(bh) * S.nitems / G);
+      afa_tc_sk_kernel<HD><<<static_cast<int>(G), C::kThreads, C::SMEM_BYTES, stream>>>(tq, tk, tv, LL, S);
+      cudaError_t e = cudaGetLastError();
+      if (e != cudaSuccess) return e;
+    }
+    if (LL.mode == kAccumFinal) {
+      long long rows = 0;
+      for (int p = 0; p < LL.nprob; ++p) rows += LL.prob[p].q.len;
+      rows *= bh;
+      long long blocks = (rows + 7) / 8;  // 8 warps (rows) per block
+      if (blocks > 8LL * sm_count[dev]) blocks = 8LL * sm_count[dev];
+      sk_finalize_kernel<HD><<<static_cast<int>(blocks), 256, 0, stream>>>(LL);
+    }
+    return cudaGetLastError();
+  }
   dim3 grid(bh, total);
   afa_tc_fwd_kernel<HD><<<grid, C::kThreads, C::SMEM_BYTES, stream>>>(tq, tk, tv, LL);
   return cudaGetLastError();

@@ -277,8 +277,11 @@ def run_ring(args, rank, world, peaks, traffic):
         "value": value,
         "ms_per_step": ms / args.steps,
         "tok_per_s": RING["L"] * RING["B"] * args.steps / (ms / 1e3),
-        "gpu_launches": kt.count(),
-        "roofline": {"bound": "tensor", "kernel": "afa_tc_fwd_kernel<128>", "achieved": achieved,
+        # One attention kernel per hop; the last hop of a ring call (FINALIZE)
+        # also launches its divide pass after the persistent accumulate kernel.
+        "gpu_launches": kt.count() + (args.steps if world > 1 else 0),
+        "roofline": {"bound": "tensor", "kernel": "afa_tc_fwd_kernel<128>" if world == 1 else
+                     "afa_tc_fwd_kernel<128> (first hop) / afa_tc_sk_kernel<128> (other hops)", "achieved": achieved,
                      "peak": peaks["bf16_tflops"], "unit": "TFLOP/s", "frac": achieved / peaks["bf16_tflops"],
                      "traffic": tr, "peak_source": peaks["source"] + " bf16_tflops (burst)",
                      "launch_ms": kernel_ms, "flops_per_launch": per_launch_flops},
