@@ -318,6 +318,32 @@ def run_ring_e2e(args, rank, world):
             "d2h_bytes_per_step": d2h, "steps": steps, "ms_per_step": ms / steps}
 
 
+def run_ring_hop(args, peaks, world=8, rank=0, hop_index=1):
+    """Profiling aid: one accumulate hop of the config-5 ring at `world` GPUs
+    (rank `rank`, hop `hop_index`), timed on this GPU with the ring's shapes."""
+    import torch
+    from algebraic_intelligence_b200.afa import hop_forward
+    from algebraic_intelligence_b200.ring import ring_plan
+    B, H, L, D = RING["B"], RING["H"], RING["L"], RING["D"]
+    s = L // world
+    gen = torch.Generator(device="cuda").manual_seed(0)
+    q, k, v = (randn_bf16((B, H, s, D), gen) for _ in range(3))
+    o_acc = torch.zeros((B, H, s, D), dtype=torch.float32, device="cuda")
+    d_acc = torch.zeros((B, H, s), dtype=torch.float32, device="cuda")
+    hop = ring_plan(rank, world, L, True, "zigzag")[hop_index]
+    flops = sum(4 * B * H * D * ql * sum(kl for _, kl, _ in segs) for _, ql, _, segs in hop.problems)
+
+    def step(i, kt):
+        f = lambda: hop_forward(q, k, v, hop.problems, True, hop.mode, o_acc=o_acc, d_acc=d_acc,  # noqa: E731
+                                sink_omega=0.5)
+        kt.around(f) if kt else f()
+
+    ms, kt = timed(step, args.steps, max(args.warmup, 1), 1)
+    achieved = flops / (kt.mean_ms() / 1e3) / 1e12
+    return {"hop": f"rank {rank} hop {hop_index} of {world}", "mode": hop.mode, "flops_per_launch": flops,
+            "launch_ms": kt.mean_ms(), "achieved_tflops": achieved, "frac": achieved / peaks["bf16_tflops"]}
+
+
 def run_prefill(cfg, args, peaks, outliers=False):
     import torch
     import algebraic_intelligence_b200 as afa
@@ -458,7 +484,7 @@ def main():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="all", choices=["all", "ring", "prefill3", "prefill2", "decode", "decode_small"],
+    ap.add_argument("--workload", default="all", choices=["all", "ring", "ring8_hop", "prefill3", "prefill2", "decode", "decode_small"],
                     help="profiling aid: run one workload only (N=1)")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     args = ap.parse_args()
@@ -477,6 +503,7 @@ def main():
 
     if args.workload != "all":
         fn = {"ring": lambda: run_ring(args, rank, world, peaks, traffic),
+              "ring8_hop": lambda: run_ring_hop(args, peaks),
               "prefill3": lambda: run_prefill(CFG3, args, peaks),
               "prefill2": lambda: run_prefill(CFG2, args, peaks, outliers=True),
               "decode": lambda: run_decode(args, peaks),
