@@ -7,7 +7,9 @@ Drop-in for the forward entry points of src/kernels/pallas_afa.py
                                    ValueError conditions and messages)
 * ``tiled_afa_forward``         -- pallas_afa.py:330-406 (the reference's XLA
                                    path; same math, so the same kernels)
-* ``pallas_afa``                -- pallas_afa.py:579-612, forward only
+* ``pallas_afa``                -- pallas_afa.py:579-615, differentiable: torch
+                                   autograd runs the analytical backward
+* ``tiled_afa_backward``        -- pallas_afa.py:409-522
 * ``algebraic_flash_attention`` -- pallas_afa.py:695-739; any sequence length,
                                    handled in-kernel by masking instead of
                                    padding copies
@@ -27,6 +29,7 @@ import ctypes
 import math
 from typing import Optional
 
+import numpy as np
 import torch
 
 from . import _lib
@@ -35,6 +38,7 @@ from ._tensors import Staged, host_checks_float
 __all__ = [
     "pallas_afa_forward",
     "tiled_afa_forward",
+    "tiled_afa_backward",
     "pallas_afa",
     "algebraic_flash_attention",
     "afa_decode",
@@ -79,6 +83,12 @@ def pallas_afa_forward(q, k, v, sink_omega: float = 0.5, causal: bool = False, b
     (the reference's Precision.HIGHEST, pallas_afa.py:224-228).
     """
     del interpret  # there is one execution path: the GPU kernels
+    _check_pallas_args(q, k, v, sink_omega, block_q, block_k, valid_seq_len)
+    return _launch_fwd(q, k, v, sink_omega, causal, valid_seq_len, return_denominator)
+
+
+def _check_pallas_args(q, k, v, sink_omega, block_q, block_k, valid_seq_len):
+    """The argument checks of pallas_afa_forward (pallas_afa.py:167-186)."""
     if q.ndim != 4 or k.ndim != 4 or v.ndim != 4:
         raise ValueError("q, k, and v must all have shape (batch, heads, sequence, dimension)")
     if tuple(q.shape) != tuple(k.shape) or tuple(q.shape) != tuple(v.shape):
@@ -97,7 +107,6 @@ def pallas_afa_forward(q, k, v, sink_omega: float = 0.5, causal: bool = False, b
     if valid_seq_len is not None and not 0 < valid_seq_len <= seq_len:
         raise ValueError("valid_seq_len must be in [1, seq_len]")
     host_checks_float(q, k, v)
-    return _launch_fwd(q, k, v, sink_omega, causal, valid_seq_len, return_denominator)
 
 
 def tiled_afa_forward(q, k, v, sink_omega: float = 0.5, causal: bool = False, block_q: int = 128,
@@ -122,13 +131,85 @@ def tiled_afa_forward(q, k, v, sink_omega: float = 0.5, causal: bool = False, bl
     return _launch_fwd(q, k, v, sink_omega, causal, valid_seq_len, return_denominator)
 
 
+def _launch_bwd(q, k, v, out, d_total, g_out, causal, valid_seq_len):
+    """dq, dk, dv through afa_bwd; all arguments are contiguous CUDA tensors."""
+    b, h, l, d = q.shape
+    code = _lib.dtype_code(q.dtype)
+    lib = _lib.load()
+    den = d_total.reshape(b, h, l).to(_lib.accum_dtype(q.dtype)).contiguous()
+    need = lib.afa_bwd_workspace_bytes(b, h, l, d, code)
+    ws = torch.empty(max(need, 1), dtype=torch.uint8, device=q.device)
+    dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+    with torch.cuda.device(q.device):
+        rc = lib.afa_bwd(q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), den.data_ptr(), g_out.data_ptr(),
+                         dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), b, h, l, d, code, int(bool(causal)),
+                         int(valid_seq_len or 0), ws.data_ptr(), need, _lib.stream_ptr(q.device))
+    _lib.check(rc, "afa_bwd")
+    return dq, dk, dv
+
+
+def tiled_afa_backward(q, k, v, out, d_total, g_out, sink_omega: float = 0.5, causal: bool = False,
+                       block_q: int = 128, block_k: int = 128, valid_seq_len: Optional[int] = None):
+    """Analytical single-pass backward (src/kernels/pallas_afa.py:409-522).
+
+    Returns (dq, dk, dv) in q's dtype: the gradients of sum(out * g_out) for
+    out = AFA(q, k, v), given the forward's ``out`` and ``d_total`` (row sum +
+    sink, from ``return_denominator=True``). As in the reference the sink
+    enters only through ``d_total`` (:429), and bfloat16 inputs round the
+    weights and score gradients to bfloat16 before the three products with fp32
+    accumulation (:440-448). ``block_q`` / ``block_k`` do not change the result.
+    """
+    del sink_omega
+    arrays = (q, k, v, out, g_out)
+    if any(a.ndim != 4 for a in arrays) or any(tuple(a.shape) != tuple(q.shape) for a in arrays):
+        raise ValueError("q, k, v, out and g_out must have the same four-dimensional shape")
+    if block_q <= 0 or block_k <= 0:
+        raise ValueError("block_q and block_k must be positive")
+    b, h, l, _ = q.shape
+    if int(np.prod(d_total.shape)) != b * h * l:
+        raise ValueError(f"d_total must hold one value per query row, shape (B, H, L, 1); got {tuple(d_total.shape)}")
+    if valid_seq_len is not None and not 0 < valid_seq_len <= l:
+        raise ValueError("valid_seq_len must be in [1, seq_len]")
+    host_checks_float(q, k, v, out, g_out)
+    st = Staged(q, k, v, out, d_total, g_out)
+    q, k, v, out, d_total, g_out = st.tensors
+    if len({t.dtype for t in (q, k, v, out, g_out)}) != 1:
+        raise TypeError("q, k, v, out and g_out must share a dtype")
+    return tuple(st.back(t) for t in _launch_bwd(q, k, v, out, d_total, g_out, causal, valid_seq_len))
+
+
+class _PallasAfa(torch.autograd.Function):
+    """pallas_afa with its analytical VJP (pallas_afa.py:532-575, :615)."""
+
+    @staticmethod
+    def forward(ctx, q, k, v, sink_omega, causal, valid_seq_len):
+        out, den = _launch_fwd(q, k, v, sink_omega, causal, valid_seq_len, True)
+        ctx.save_for_backward(q, k, v, out, den)
+        ctx.causal, ctx.valid_seq_len = causal, valid_seq_len
+        return out
+
+    @staticmethod
+    def backward(ctx, g_out):
+        q, k, v, out, den = ctx.saved_tensors
+        dq, dk, dv = _launch_bwd(q, k, v, out, den, g_out.contiguous(), ctx.causal, ctx.valid_seq_len)
+        return dq, dk, dv, None, None, None
+
+
 def pallas_afa(q, k, v, sink_omega: float = 0.5, causal: bool = False, block_q: int = 128, block_k: int = 128,
                valid_seq_len: Optional[int] = None):
-    """Forward of the reference's custom-VJP entry (src/kernels/pallas_afa.py:579-612).
+    """The reference's custom-VJP entry (src/kernels/pallas_afa.py:579-615).
 
-    The analytical backward (pallas_afa.py:409-522) is not part of this build;
-    the returned tensor carries no autograd graph.
+    Same forward as ``pallas_afa_forward``. For CUDA tensors that require
+    gradients the result is differentiable: torch autograd calls the analytical
+    backward (``tiled_afa_backward``), as jax.grad does through ``defvjp``.
     """
+    if any(isinstance(t, torch.Tensor) and t.requires_grad for t in (q, k, v)):
+        # The forward's argument checks, before anything is recorded.
+        _check_pallas_args(q, k, v, sink_omega, block_q, block_k, valid_seq_len)
+        if not (q.is_cuda and k.is_cuda and v.is_cuda):
+            raise ValueError("a differentiable pallas_afa needs CUDA tensors")
+        return _PallasAfa.apply(q.contiguous(), k.contiguous(), v.contiguous(), float(sink_omega), bool(causal),
+                                valid_seq_len)
     return pallas_afa_forward(q, k, v, sink_omega=sink_omega, causal=causal, block_q=block_q, block_k=block_k,
                               valid_seq_len=valid_seq_len)
 

@@ -12,6 +12,11 @@
  *                            through valid_len, algebraic_flash_attention (:695-739)
  *   afa_fwd_hop           <- one hop of distributed_ring_afa (pallas_afa.py:634-654)
  *   afa_finalize          <- the ring's final divide (pallas_afa.py:661)
+ *   afa_ring_export/open/pull/close
+ *                         <- the K/V transport of the ring, lax.ppermute
+ *                            (pallas_afa.py:651-652)
+ *   afa_bwd               <- tiled_afa_backward (pallas_afa.py:409-522), the VJP
+ *                            of pallas_afa (:555-615)
  *   afa_decode            <- no reference counterpart: exact AFA for one query
  *                            token over a KV cache (pallas_afa_forward with Lq=1)
  *   algebraic_softmax_fwd <- algebraic_softmax   (src/attention.py:88-91, :59-67)
@@ -128,8 +133,9 @@ AFA_API int afa_finalize(const void* o_acc, const void* d_acc, void* out, void* 
  * maps with CUDA IPC; a hop then pulls the shard it needs straight from the
  * owning rank with the copy engines over NVLink, so the transfer uses no SMs
  * and overlaps the previous hop's kernel. Ordering between ranks (publish
- * before pull, pull before overwrite) is the caller's: the Python ring inserts
- * one stream-ordered barrier per call.
+ * before pull, pull before overwrite or free) is the caller's: the Python ring
+ * inserts two stream-ordered barriers per call, after publishing and at the
+ * end.
  *
  *   afa_ring_export  IPC handle (AFA_RING_HANDLE_BYTES bytes, written to
  *                    handle_out) of the device allocation that holds ptr, and
@@ -146,6 +152,21 @@ AFA_API int afa_ring_export(const void* ptr, void* handle_out, unsigned long lon
 AFA_API int afa_ring_open(const void* handle, void** base_out);
 AFA_API int afa_ring_close(void* base);
 AFA_API int afa_ring_pull(void* dst, const void* src, size_t bytes, void* stream);
+
+/*
+ * Backward (tiled_afa_backward, pallas_afa.py:409-522; the VJP of pallas_afa,
+ * :555-575): dq, dk, dv of sum(out * g_out) for out = afa_fwd(q, k, v).
+ *   q, k, v, out, g_out, dq, dk, dv  (B, H, L, D) in `dtype` (bf16, f32, f64)
+ *   d_total   (B, H, L) from afa_fwd: row sum + sink, float32 (float64 for f64)
+ *   causal, valid_len as afa_fwd (valid_len 0 = L)
+ *   workspace afa_bwd_workspace_bytes(B, H, L, D, dtype) bytes of device
+ *             scratch (the per-row E = sum(g_out * out)), caller-owned.
+ * The sink enters only through d_total, as in the reference (:429).
+ */
+AFA_API int afa_bwd(const void* q, const void* k, const void* v, const void* out, const void* d_total,
+                    const void* g_out, void* dq, void* dk, void* dv, int B, int H, int L, int D, int dtype,
+                    int causal, int valid_len, void* workspace, size_t workspace_bytes, void* stream);
+AFA_API size_t afa_bwd_workspace_bytes(int B, int H, int L, int D, int dtype);
 
 /*
  * Decode step (no reference counterpart; the math of pallas_afa_forward with a

@@ -33,6 +33,14 @@ It restates, in float64 NumPy, the reference's own ground truth
 * ``decode``           -- exact AFA for one query token over a KV cache; the
                           reference has no decode kernel, so its oracle is
                           ``afa`` with Lq = 1, non-causal.
+* ``afa_backward``     -- gradients of sum(afa(q, k, v) * g_out) by the
+                          analytical single-pass backward of
+                          src/kernels/pallas_afa.py:409-522
+                          (``tiled_afa_backward``), in query-row blocks. The
+                          reference pins it against JAX autodiff
+                          (tests/test_pallas_afa.py:292-322); JAX is absent
+                          here, so ``tests/test_oracle.py`` pins it against
+                          central finite differences of ``afa``.
 
 Parity is pinned by ``tests/test_oracle.py`` against golden vectors that
 ``tests/golden/make_golden.py`` produced by importing the reference's own
@@ -53,6 +61,7 @@ __all__ = [
     "ring_simulation",
     "zigzag_chunks",
     "decode",
+    "afa_backward",
     "rel_err",
 ]
 
@@ -157,6 +166,53 @@ def afa_blocked(q, k, v, sink=0.5, causal=False, q_pos0=0, k_pos0=0,
         return num, rsum
     denom = rsum + sink
     return num / denom, denom
+
+
+def afa_backward(q, k, v, g_out, sink=0.5, causal=False, valid_len=None, block=512):
+    """(dq, dk, dv) of sum(afa(q, k, v) * g_out) in float64.
+
+    Restates tiled_afa_backward (src/kernels/pallas_afa.py:409-522):
+      E_i   = sum_d g_out[i, d] * out[i, d]                  (:459)
+      w_ij  = rho(s_ij)^8 / D_i, D_i = row_sum + sink         (:475-499)
+      g_w   = g_out_i . v_j                                   (:500)
+      ds_ij = 8 * scale * r_ij * w_ij * (g_w,ij - E_i),
+              r = 1 / sqrt(1 + s^2)                           (:502)
+      dq = ds k, dk = ds^T q, dv = w^T g_out                  (:507-510)
+    with the forward's masks (causal key_pos <= query_pos, keys at index >=
+    valid_len dropped). Query and key positions start at 0 (square attention,
+    as the reference's backward).
+    """
+    q = np.asarray(q, dtype=np.float64)
+    k = np.asarray(k, dtype=np.float64)
+    v = np.asarray(v, dtype=np.float64)
+    g = np.asarray(g_out, dtype=np.float64)
+    lq, lk = q.shape[-2], k.shape[-2]
+    scale = 1.0 / np.sqrt(q.shape[-1])
+    limit = lk if valid_len is None else min(int(valid_len), lk)
+    key_ok = np.arange(lk) < limit
+    kt = np.swapaxes(k, -1, -2)
+    vt = np.swapaxes(v, -1, -2)
+    dq = np.zeros_like(q)
+    dk = np.zeros_like(k)
+    dv = np.zeros_like(v)
+    for start in range(0, lq, block):
+        sel = np.arange(start, min(start + block, lq))
+        qb, gb = q[..., sel, :], g[..., sel, :]
+        s = np.matmul(qb, kt) * scale
+        visible = np.broadcast_to(key_ok, (len(sel), lk))
+        if causal:
+            visible = visible & (np.arange(lk)[None, :] <= sel[:, None])
+        p = np.where(visible, octic(s), 0.0)
+        denom = p.sum(axis=-1, keepdims=True) + sink
+        w = p / denom
+        out = np.matmul(w, v)
+        e = np.sum(gb * out, axis=-1, keepdims=True)
+        r = 1.0 / np.sqrt(1.0 + s * s)
+        ds = 8.0 * scale * r * w * (np.matmul(gb, vt) - e)
+        dq[..., sel, :] = np.matmul(ds, k)
+        dk += np.matmul(np.swapaxes(ds, -1, -2), qb)
+        dv += np.matmul(np.swapaxes(w, -1, -2), gb)
+    return dq, dk, dv
 
 
 def zigzag_chunks(rank, world):

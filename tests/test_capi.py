@@ -108,3 +108,18 @@ def test_ring_exchange_argument_checks():
     assert lib.afa_ring_pull(None, 1, 16, None) == _lib.AFA_ERR_INVALID
     assert b"afa_ring_pull" in lib.afa_last_error()
     assert lib.afa_ring_pull(None, None, 0, None) == _lib.AFA_OK
+
+
+def test_backward_argument_checks():
+    """afa_bwd validates before any CUDA call: dtype, null pointers, shapes,
+    and the workspace size it asks for through afa_bwd_workspace_bytes."""
+    lib = _lib.load()
+    ptrs = [1] * 9
+    assert lib.afa_bwd_workspace_bytes(2, 3, 100, 64, _lib.AFA_F32) == 2 * 3 * 100 * 4
+    assert lib.afa_bwd_workspace_bytes(2, 3, 100, 64, _lib.AFA_F64) == 2 * 3 * 100 * 8
+    assert lib.afa_bwd(*ptrs, 1, 1, 64, 64, _lib.AFA_F16, 0, 0, 1, 1 << 20, None) == _lib.AFA_ERR_DTYPE
+    assert lib.afa_bwd(None, *ptrs[1:], 1, 1, 64, 64, _lib.AFA_BF16, 0, 0, 1, 1 << 20, None) == _lib.AFA_ERR_INVALID
+    assert lib.afa_bwd(*ptrs, 1, 1, 64, 512, _lib.AFA_BF16, 0, 0, 1, 1 << 20, None) == _lib.AFA_ERR_INVALID
+    assert lib.afa_bwd(*ptrs, 1, 1, 64, 64, _lib.AFA_BF16, 0, 65, 1, 1 << 20, None) == _lib.AFA_ERR_INVALID
+    assert lib.afa_bwd(*ptrs, 1, 1, 64, 64, _lib.AFA_BF16, 0, 0, 1, 16, None) == _lib.AFA_ERR_INVALID
+    assert b"workspace" in lib.afa_last_error()

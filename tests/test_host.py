@@ -80,6 +80,22 @@ def test_unified_entry_value_errors():
         afa.algebraic_flash_attention(_x((1, 1, 64, 8)), _x((1, 1, 64, 8)), _x((1, 1, 64, 8)), block_k=-1)
 
 
+def test_backward_argument_errors():
+    x = _x((1, 1, 64, 8))
+    d = np.ones((1, 1, 64, 1), dtype=np.float32)
+    with pytest.raises(ValueError, match="same four-dimensional shape"):
+        afa.tiled_afa_backward(x, x, x, _x((1, 1, 63, 8)), d, x)
+    with pytest.raises(ValueError, match="positive"):
+        afa.tiled_afa_backward(x, x, x, x, d, x, block_q=0)
+    with pytest.raises(ValueError, match="d_total"):
+        afa.tiled_afa_backward(x, x, x, x, np.ones((1, 1, 32, 1), dtype=np.float32), x)
+    with pytest.raises(ValueError, match="valid_seq_len"):
+        afa.tiled_afa_backward(x, x, x, x, d, x, valid_seq_len=65)
+    xi = np.ones((1, 1, 64, 8), dtype=np.int32)
+    with pytest.raises(TypeError):
+        afa.tiled_afa_backward(xi, xi, xi, xi, d, xi)
+
+
 # ---------------------------------------------------------------------------
 # Ring plan
 # ---------------------------------------------------------------------------

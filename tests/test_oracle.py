@@ -106,3 +106,46 @@ def test_ring_simulation_equals_global(world, causal, zigzag):
     q, k, v = (rng.normal(size=(1, 2, 24 * world, 8)) for _ in range(3))
     ring = orc.ring_simulation(q, k, v, world, causal=causal, zigzag=zigzag)
     assert orc.rel_err(ring, orc.afa(q, k, v, causal=causal)) <= 1e-12
+
+
+# ---------------------------------------------------------------------------
+# Backward oracle, pinned by finite differences of the pinned forward
+# ---------------------------------------------------------------------------
+@pytest.mark.parametrize("causal,valid_len", [(False, None), (True, None), (False, 11), (True, 13)])
+def test_backward_oracle_matches_finite_differences(causal, valid_len):
+    """afa_backward restates tiled_afa_backward (pallas_afa.py:409-522). The
+    reference checks it against JAX autodiff of the exact forward
+    (tests/test_pallas_afa.py:292-322, 1e-5); here central differences of the
+    golden-pinned float64 forward play that role."""
+    rng = np.random.default_rng(3)
+    shape = (1, 2, 16, 8)
+    q, k, v, g = (rng.standard_normal(shape) for _ in range(4))
+
+    def loss(q_, k_, v_):
+        if valid_len is None:
+            out = orc.afa(q_, k_, v_, causal=causal)
+        else:
+            out, _ = orc.afa_blocked(q_, k_, v_, causal=causal, valid_len=valid_len)
+        return float(np.sum(out * g))
+
+    dq, dk, dv = orc.afa_backward(q, k, v, g, causal=causal, valid_len=valid_len)
+    h = 1e-6
+    for name, arr, grad in (("q", q, dq), ("k", k, dk), ("v", v, dv)):
+        for idx in [tuple(rng.integers(0, n) for n in shape) for _ in range(12)]:
+            plus, minus = arr.copy(), arr.copy()
+            plus[idx] += h
+            minus[idx] -= h
+            args_p = {"q": q, "k": k, "v": v}
+            args_m = dict(args_p)
+            args_p[name], args_m[name] = plus, minus
+            fd = (loss(**{x + "_": a for x, a in args_p.items()}) - loss(**{x + "_": a for x, a in args_m.items()})) / (2 * h)
+            assert abs(fd - grad[idx]) <= 1e-6 * max(1.0, np.abs(grad).max()), (name, idx, fd, grad[idx])
+
+
+def test_backward_oracle_blocking_is_exact():
+    rng = np.random.default_rng(4)
+    q, k, v, g = (rng.standard_normal((2, 1, 40, 16)) for _ in range(4))
+    a = orc.afa_backward(q, k, v, g, causal=True, block=7)
+    b = orc.afa_backward(q, k, v, g, causal=True, block=512)
+    for x, y in zip(a, b):
+        assert np.max(np.abs(x - y)) <= 1e-12 * np.max(np.abs(y))
