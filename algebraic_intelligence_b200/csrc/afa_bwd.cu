@@ -11,7 +11,9 @@
 // before the three products (the reference casts both matmul operands to the
 // input dtype, :440-448); float32 and float64 stay at full precision.
 //
-// CUDA-core path (every dtype and head dimension up to 256). Two kernels, no
+// bf16 with head_dim 64 or 128 runs on the tensor cores (afa_bwd_tc.cu); this
+// file holds the CUDA-core path (every dtype and head dimension up to 256),
+// the row-dot kernel both paths use, and the C ABI. Two kernels, no
 // atomics: a query-parallel kernel recomputes S and g = g_out v^T for its rows
 // against every visible key tile and accumulates dq; a key-parallel kernel
 // recomputes them for its keys against every query tile that sees them and
@@ -364,14 +366,16 @@ cudaError_t launch_bwd_cfg(const BwdArgs& a, int bh, cudaStream_t stream) {
 }
 
 template <typename T, typename A>
+cudaError_t launch_rowdot(const BwdArgs& a, cudaStream_t stream) {
+  long long blocks = (a.rows * 32 + 255) / 256;
+  if (blocks > 148LL * 16) blocks = 148LL * 16;
+  bwd_rowdot_kernel<T, A><<<static_cast<int>(blocks), 256, 0, stream>>>(a);
+  return cudaGetLastError();
+}
+
+template <typename T, typename A>
 cudaError_t launch_bwd_typed(const BwdArgs& a, int bh, cudaStream_t stream) {
-  {
-    long long blocks = (a.rows * 32 + 255) / 256;
-    if (blocks > 148LL * 16) blocks = 148LL * 16;
-    bwd_rowdot_kernel<T, A><<<static_cast<int>(blocks), 256, 0, stream>>>(a);
-    cudaError_t e = cudaGetLastError();
-    if (e != cudaSuccess) return e;
-  }
+  if (cudaError_t e = launch_rowdot<T, A>(a, stream); e != cudaSuccess) return e;
   if constexpr (sizeof(A) == 8) {
     if (a.D <= 128) return launch_bwd_cfg<T, A, 32, 32, 128>(a, bh, stream);
     return launch_bwd_cfg<T, A, 16, 16, 256>(a, bh, stream);
@@ -434,6 +438,23 @@ extern "C" int afa_bwd(const void* q, const void* k, const void* v, const void* 
   const int bh = B * H;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   cudaError_t e;
+  if (tc_bwd_supported(dtype, D)) {
+    // Tensor cores: E first, then the key-parallel dK/dV and query-parallel dQ kernels.
+    int* status = device_status_ptr();
+    if (!status) return set_last_error(AFA_ERR_CUDA, "afa_bwd: could not resolve the device status word");
+    const char* detail = nullptr;
+    e = launch_rowdot<__nv_bfloat16, float>(a, s);
+    if (e == cudaSuccess)
+      e = launch_tc_bwd(q, k, v, g_out, static_cast<const float*>(d_total), static_cast<const float*>(workspace), dq,
+                        dk, dv, B, H, L, D, a.causal, a.valid, a.scale, status, s, &detail);
+    if (e != cudaSuccess) {
+      char msg[256];
+      snprintf(msg, sizeof(msg), "afa_bwd tensor-core launch: %s%s%s", cudaGetErrorString(e), detail ? " -- " : "",
+               detail ? detail : "");
+      return set_last_error(AFA_ERR_CUDA, msg);
+    }
+    return AFA_OK;
+  }
   if (dtype == AFA_F64)
     e = launch_bwd_typed<double, double>(a, bh, s);
   else if (dtype == AFA_F32)

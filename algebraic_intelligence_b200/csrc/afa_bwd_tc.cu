@@ -1,0 +1,517 @@
+// AFA backward on the tcgen05 tensor cores (bf16 inputs, head_dim 64 or 128).
+//
+// Same math as afa_bwd.cu (tiled_afa_backward, src/kernels/pallas_afa.py:
+// 409-522): w = rho(s)^8 / d_total, ds = 8 scale r w (g_out.v - E),
+// dq = ds k, dk = ds^T q, dv = w^T g_out, with w and ds rounded to bf16 before
+// the products (:440-448) and fp32 accumulation. rho uses the single-MUFU form
+// of the forward kernel (rho = (1+s^2) rsqrt(1+s^2) + s), whose rsqrt is also
+// the r of the score derivative.
+//
+// Two kernels, each with the forward's warp roles (576 threads: 16 "grad"
+// warps, 1 TMA warp, 1 MMA-issue warp) and one CTA per SM:
+//
+//   afa_bwd_dkv_tc_kernel  one 128-key tile per CTA, looping over the query
+//     tiles that see it. TMEM holds S^T = K Q^T and dP^T = V dO^T (keys on the
+//     lanes), then dV and dK. A thread owns one key (one TMEM lane); warpgroup g
+//     owns query columns [32g, 32g+32). It turns its S^T and dP^T columns into
+//     W^T and dS^T, written back as packed bf16 over the first half of the
+//     columns it read, which is the A operand layout of the next two MMAs:
+//     dV += W^T dO and dK += dS^T Q (B = the dO / Q tile read MN-major, the
+//     same shared-memory tile the S^T MMA read K-major).
+//   afa_bwd_dq_tc_kernel   one 128-query tile per CTA, looping over visible key
+//     tiles: S = Q K^T and dP = dO V^T, then dQ += dS K with dS from TMEM
+//     (queries on the lanes, per-row 1/d_total and E in registers).
+//
+// TMEM columns: X (S^T or S) [0,128), Y (dP^T or dP) [128,256), accumulators
+// from 256. K/Q/V/dO tiles are TMA-loaded with 128-byte swizzle, no multicast.
+// Every wait is bounded (afa_common.cuh) and reports to the device status word.
+#include <cstdio>
+
+#include "afa_b200.h"
+#include "afa_common.cuh"
+#include "afa_internal.h"
+#include "afa_tmap.h"
+
+namespace afa {
+namespace {
+
+template <int HD>
+struct BwdCfg {
+  static constexpr int kTmaWarp = 16;
+  static constexpr int kMmaWarp = 17;
+  static constexpr int kThreads = 18 * 32;
+  static constexpr int KSUB = HD / 64;
+  static constexpr int SUB_BYTES = 128 * 128;
+  static constexpr int TILE_BYTES = KSUB * SUB_BYTES;  // 128 rows x HD bf16
+  static constexpr int NST = 2;                        // stages of the streamed tile pair
+  static constexpr int FIX_OFF = 0;                    // the CTA's two fixed tiles
+  static constexpr int ST_OFF = 2 * TILE_BYTES;
+  static constexpr int VEC_OFF = ST_OFF + NST * 2 * TILE_BYTES;  // per grad warp: 32 x (1/d, E) floats
+  static constexpr int BAR_OFF = VEC_OFF + 16 * 64 * 4;
+  static constexpr int NBAR = 1 + 2 * NST + 4;  // fix_full, st_full[], st_empty[], s_full, g_full, o_full, drain
+  static constexpr int SMEM_BYTES = BAR_OFF + NBAR * 8 + 16 + 1024;
+  static constexpr uint32_t TMEM_COLS = 512;
+  static constexpr uint32_t X_COL = 0, Y_COL = 128, ACC0 = 256, ACC1 = 256 + HD;
+  __device__ static constexpr uint32_t p_col(int kk) {
+    return static_cast<uint32_t>((kk >> 1) * 32 + (kk & 1) * 8);
+  }
+};
+
+struct BwdTcArgs {
+  const float* dtot;  // (B, H, L) d_total
+  const float* e;     // (B, H, L) E
+  __nv_bfloat16* dq;
+  __nv_bfloat16* dk;
+  __nv_bfloat16* dv;
+  int* status;
+  int L, causal, valid;
+  float scale;
+};
+
+struct Bars {
+  uint64_t *fix_full, *st_full, *st_empty, *s_full, *g_full, *o_full, *drain;
+  uint32_t* tmem_slot;
+};
+
+template <int HD>
+__device__ __forceinline__ Bars carve(uint8_t* smem) {
+  using C = BwdCfg<HD>;
+  Bars b;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::BAR_OFF);
+  b.fix_full = bars;
+  b.st_full = bars + 1;
+  b.st_empty = b.st_full + C::NST;
+  b.s_full = b.st_empty + C::NST;
+  b.g_full = b.s_full + 1;
+  b.o_full = b.g_full + 1;
+  b.drain = b.o_full + 1;
+  b.tmem_slot = reinterpret_cast<uint32_t*>(b.drain + 1);
+  return b;
+}
+
+template <int HD>
+__device__ __forceinline__ uint32_t setup(uint8_t* smem, const Bars& b, const CUtensorMap* t0, const CUtensorMap* t1,
+                                          const CUtensorMap* t2, const CUtensorMap* t3) {
+  using C = BwdCfg<HD>;
+  const int warp = threadIdx.x >> 5;
+  if (threadIdx.x == 0) {
+    mbar_init(b.fix_full, 1);
+    for (int s = 0; s < C::NST; ++s) {
+      mbar_init(b.st_full + s, 1);
+      mbar_init(b.st_empty + s, 1);
+    }
+    mbar_init(b.s_full, 1);
+    mbar_init(b.g_full, 16);  // one elected arrive per grad warp
+    mbar_init(b.o_full, 1);
+    mbar_init(b.drain, 1);
+    fence_barrier_init();
+    fence_proxy_async_smem();
+    prefetch_tmap(t0);
+    prefetch_tmap(t1);
+    prefetch_tmap(t2);
+    prefetch_tmap(t3);
+  }
+  if (warp == C::kMmaWarp) {
+    tmem_alloc(b.tmem_slot, C::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  return *b.tmem_slot;
+}
+
+// TMA producer: the two fixed tiles (rows fix_row), then `niter` pairs of
+// streamed tiles (rows st_row0 + 128 * it) through NST stages.
+template <int HD>
+__device__ __forceinline__ void produce(uint8_t* smem, const Bars& b, const CUtensorMap* fa, const CUtensorMap* fb,
+                                        const CUtensorMap* sa, const CUtensorMap* sb, int fix_row, int st_row0,
+                                        int niter, int bh, int* status) {
+  using C = BwdCfg<HD>;
+  if (niter <= 0) return;
+  mbar_arrive_expect_tx(b.fix_full, 2 * C::TILE_BYTES);
+  for (int h = 0; h < C::KSUB; ++h) {
+    tma_load_3d(smem + C::FIX_OFF + h * C::SUB_BYTES, fa, b.fix_full, 64 * h, fix_row, bh);
+    tma_load_3d(smem + C::FIX_OFF + C::TILE_BYTES + h * C::SUB_BYTES, fb, b.fix_full, 64 * h, fix_row, bh);
+  }
+  int issued = 0;
+  for (int it = 0; it < niter; ++it) {
+    const int s = it % C::NST;
+    if (!mbar_wait(b.st_empty + s, ((it / C::NST) & 1) ^ 1, status, kDevTimeoutProducer)) break;
+    mbar_arrive_expect_tx(b.st_full + s, 2 * C::TILE_BYTES);
+    uint8_t* base = smem + C::ST_OFF + s * 2 * C::TILE_BYTES;
+    for (int h = 0; h < C::KSUB; ++h) {
+      tma_load_3d(base + h * C::SUB_BYTES, sa, b.st_full + s, 64 * h, st_row0 + 128 * it, bh);
+      tma_load_3d(base + C::TILE_BYTES + h * C::SUB_BYTES, sb, b.st_full + s, 64 * h, st_row0 + 128 * it, bh);
+    }
+    issued = it + 1;
+  }
+  // Do not leave the CTA while loads into its shared memory are in flight.
+  (void)mbar_wait(b.fix_full, 0, nullptr, 0);
+  for (int it = issued - C::NST < 0 ? 0 : issued - C::NST; it < issued; ++it)
+    (void)mbar_wait(b.st_full + (it % C::NST), (it / C::NST) & 1, nullptr, 0);
+}
+
+// MMA issuer. Per iteration: X = F0 S0^T and Y = F1 S1^T (F = fixed tiles,
+// S = streamed tiles, both K-major), then, once the grad warps have written
+// the packed bf16 operands, ACC0 += X' M0 and (if two products) ACC1 += Y' M1,
+// where M0/M1 are streamed tiles read MN-major.
+//   dK/dV kernel: F = (K, V), S = (Q, dO): ACC0 = dV += W^T dO, ACC1 = dK += dS^T Q.
+//   dQ kernel:    F = (Q, dO), S = (K, V): ACC0 = dQ += dS K (one product).
+template <int HD, bool TWO>
+__device__ __forceinline__ void issue(uint8_t* smem, const Bars& b, uint32_t tmem, int niter, int* status) {
+  using C = BwdCfg<HD>;
+  if (niter <= 0) return;
+  constexpr uint32_t idesc_x = idesc_bf16_f32(128, 128, false);
+  constexpr uint32_t idesc_acc = idesc_bf16_f32(128, HD, true);
+  const uint32_t fix = smem_u32(smem + C::FIX_OFF);
+  bool ok = mbar_wait(b.fix_full, 0, status, kDevTimeoutMma);
+  for (int it = 0; ok && it < niter; ++it) {
+    const int s = it % C::NST;
+    if (!(ok = mbar_wait(b.st_full + s, (it / C::NST) & 1, status, kDevTimeoutMma))) break;
+    tc_fence_after();
+    const uint32_t st = smem_u32(smem + C::ST_OFF + s * 2 * C::TILE_BYTES);
+#pragma unroll
+    for (int t = 0; t < 2; ++t) {
+#pragma unroll
+      for (int kk = 0; kk < HD / 16; ++kk) {
+        const uint32_t off = (kk >> 2) * C::SUB_BYTES + (kk & 3) * 32;
+        const uint64_t a = sw128_desc(fix + t * C::TILE_BYTES + off, 16, 1024);
+        const uint64_t bd = sw128_desc(st + t * C::TILE_BYTES + off, 16, 1024);
+        umma_ss(tmem + (t ? C::Y_COL : C::X_COL), a, bd, idesc_x, kk > 0 ? 1u : 0u);
+      }
+    }
+    umma_commit(b.s_full);
+    if (!(ok = mbar_wait(b.g_full, it & 1, status, kDevTimeoutMma))) break;
+    tc_fence_after();
+    // dK/dV: ACC0 (dV) from X' = W^T against dO (the second streamed tile),
+    // ACC1 (dK) from Y' = dS^T against Q (the first). dQ: ACC0 from X' = dS
+    // against K (the first streamed tile).
+#pragma unroll
+    for (int kk = 0; kk < 8; ++kk) {
+      const uint64_t m0 = sw128_desc(st + (TWO ? C::TILE_BYTES : 0) + kk * 2048, C::SUB_BYTES, 1024);
+      umma_ts(tmem + C::ACC0, tmem + C::X_COL + C::p_col(kk), m0, idesc_acc, (it > 0 || kk > 0) ? 1u : 0u);
+    }
+    if constexpr (TWO) {
+#pragma unroll
+      for (int kk = 0; kk < 8; ++kk) {
+        const uint64_t m1 = sw128_desc(st + kk * 2048, C::SUB_BYTES, 1024);
+        umma_ts(tmem + C::ACC1, tmem + C::Y_COL + C::p_col(kk), m1, idesc_acc, (it > 0 || kk > 0) ? 1u : 0u);
+      }
+    }
+    umma_commit(b.st_empty + s);
+  }
+  if (ok) umma_commit(b.o_full);
+  // Every MMA this thread issued must finish before TMEM is released.
+  umma_commit(b.drain);
+  (void)mbar_wait(b.drain, 0, nullptr, 0);
+}
+
+// One 32-column chunk: scores x (raw S or S^T accumulator words), score
+// gradients y (dP or dP^T); per-column (dK/dV kernel) or per-row (dQ kernel)
+// 1/d_total and E. Writes packed bf16 W (if want_w) and dS.
+template <bool MASK, bool PER_COL>
+__device__ __forceinline__ void grad_chunk(const uint32_t (&x)[32], const uint32_t (&y)[32], uint32_t (&wp)[16],
+                                           uint32_t (&dp)[16], float scale, const float* inv_c, const float* e_c,
+                                           float inv_r, float e_r, int vis_lim, bool vis_row, int causal,
+                                           int row_pos, int col_pos0, bool row_is_key) {
+  const float c8 = 8.0f * scale;
+#pragma unroll
+  for (int c = 0; c < 32; c += 2) {
+    float wv[2], dv[2];
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      const float s = __uint_as_float(x[c + u]) * scale;
+      const float rad = fmaf(s, s, 1.0f);
+      const float r = rsqrt_approx(rad);
+      const float rho = fmaf(rad, r, s);
+      const float p2 = rho * rho;
+      const float p4 = p2 * p2;
+      const float inv = PER_COL ? inv_c[c + u] : inv_r;
+      const float ev = PER_COL ? e_c[c + u] : e_r;
+      float w = p4 * p4 * inv;
+      float ds = c8 * (r * w) * (__uint_as_float(y[c + u]) - ev);
+      if (MASK) {
+        const int col = col_pos0 + c + u;
+        // row_is_key: the row is a key, the column a query; otherwise the reverse.
+        const int key = row_is_key ? row_pos : col;
+        const int qry = row_is_key ? col : row_pos;
+        const bool vis = vis_row && key < vis_lim && (!causal || key <= qry);
+        w = vis ? w : 0.0f;
+        ds = vis ? ds : 0.0f;
+      }
+      wv[u] = w;
+      dv[u] = ds;
+    }
+    wp[c >> 1] = pack_bf16x2(wv[0], wv[1]);
+    dp[c >> 1] = pack_bf16x2(dv[0], dv[1]);
+  }
+}
+
+template <int HD>
+__global__ void __launch_bounds__(576, 1)
+    afa_bwd_dkv_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_g,
+                          const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
+                          const __grid_constant__ BwdTcArgs A) {
+  using C = BwdCfg<HD>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const Bars b = carve<HD>(smem);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int bh = blockIdx.x;
+  const int k0 = blockIdx.y * 128;  // keys with the most causal queries first
+  const int i_first = A.causal ? blockIdx.y : 0;
+  const int nq = (A.L + 127) / 128;
+  const int niter = k0 >= A.valid ? 0 : nq - i_first;
+  const uint32_t tmem = setup<HD>(smem, b, &tm_q, &tm_g, &tm_k, &tm_v);
+
+  if (warp == C::kTmaWarp) {
+    if (lane == 0) produce<HD>(smem, b, &tm_k, &tm_v, &tm_q, &tm_g, k0, 128 * i_first, niter, bh, A.status);
+  } else if (warp == C::kMmaWarp) {
+    if (lane == 0) issue<HD, true>(smem, b, tmem, niter, A.status);
+  } else {
+    const int g = warp >> 2, sub = warp & 3;
+    const int row = sub * 32 + lane;
+    const int key = k0 + row;
+    const uint32_t lane_off = static_cast<uint32_t>(sub * 32) << 16;
+    float* vec = reinterpret_cast<float*>(smem + C::VEC_OFF) + warp * 64;
+    const long long rbase = static_cast<long long>(bh) * A.L;
+    bool ok = true;
+    for (int it = 0; ok && it < niter; ++it) {
+      const int q0 = 128 * (i_first + it);
+      const int qc0 = q0 + 32 * g;
+      {  // 1/d_total and E of this warp's 32 query columns
+        const int qi = qc0 + lane;
+        const bool in = qi < A.L;
+        vec[lane] = in ? 1.0f / A.dtot[rbase + qi] : 0.0f;
+        vec[32 + lane] = in ? A.e[rbase + qi] : 0.0f;
+        __syncwarp();
+      }
+      ok = mbar_wait(b.s_full, it & 1, A.status, kDevTimeoutSoftmax);
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok) break;
+      tc_fence_after();
+      uint32_t x[32], y[32], wp[16], dp[16];
+      tmem_ld32(tmem + C::X_COL + lane_off + 32 * g, x);
+      tmem_ld32(tmem + C::Y_COL + lane_off + 32 * g, y);
+      tmem_ld_wait();
+      const bool need_mask = k0 + 127 >= A.valid || q0 + 127 >= A.L || (A.causal && q0 < k0 + 127);
+      // Columns past L read 1/d = 0, which zeroes W and dS; the mask covers
+      // invisible keys and causal order.
+      if (need_mask)
+        grad_chunk<true, true>(x, y, wp, dp, A.scale, vec, vec + 32, 0.f, 0.f, A.valid, key < A.L, A.causal, key,
+                               qc0, true);
+      else
+        grad_chunk<false, true>(x, y, wp, dp, A.scale, vec, vec + 32, 0.f, 0.f, 0, true, 0, 0, 0, true);
+      tmem_st16(tmem + C::X_COL + lane_off + 32 * g, wp);
+      tmem_st16(tmem + C::Y_COL + lane_off + 32 * g, dp);
+      tmem_st_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(b.g_full);
+    }
+    // Epilogue: warpgroup g stores columns [HD/4 g, HD/4 (g+1)) of dV and dK.
+    constexpr int OC = HD / 4;
+    bool have = niter > 0 && ok;
+    if (have) {
+      have = mbar_wait(b.o_full, 0, A.status, kDevTimeoutEpilogue);
+      have = __all_sync(0xffffffffu, have);
+    }
+    tc_fence_after();
+#pragma unroll
+    for (int t = 0; t < 2; ++t) {
+      uint32_t ov[32];
+      __syncwarp();
+      if (have) {
+        const uint32_t o_tm = tmem + (t ? C::ACC1 : C::ACC0) + lane_off + OC * g;
+        if constexpr (OC == 32) {
+          tmem_ld32(o_tm, ov);
+        } else {
+          uint32_t (&ov16)[16] = *reinterpret_cast<uint32_t(*)[16]>(ov);
+          tmem_ld16(o_tm, ov16);
+        }
+        tmem_ld_wait();
+      } else {
+#pragma unroll
+        for (int c = 0; c < 32; ++c) ov[c] = 0u;
+      }
+      if (key < A.L && (have || niter == 0)) {
+        __nv_bfloat16* dst = (t ? A.dk : A.dv) + (rbase + key) * HD + OC * g;
+#pragma unroll
+        for (int w8 = 0; w8 < OC / 8; ++w8) {
+          uint4 pkt;
+          pkt.x = pack_bf16x2(__uint_as_float(ov[8 * w8 + 0]), __uint_as_float(ov[8 * w8 + 1]));
+          pkt.y = pack_bf16x2(__uint_as_float(ov[8 * w8 + 2]), __uint_as_float(ov[8 * w8 + 3]));
+          pkt.z = pack_bf16x2(__uint_as_float(ov[8 * w8 + 4]), __uint_as_float(ov[8 * w8 + 5]));
+          pkt.w = pack_bf16x2(__uint_as_float(ov[8 * w8 + 6]), __uint_as_float(ov[8 * w8 + 7]));
+          reinterpret_cast<uint4*>(dst)[w8] = pkt;
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == C::kMmaWarp) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem, C::TMEM_COLS);
+  }
+}
+
+template <int HD>
+__global__ void __launch_bounds__(576, 1)
+    afa_bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_g,
+                         const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
+                         const __grid_constant__ BwdTcArgs A) {
+  using C = BwdCfg<HD>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const Bars b = carve<HD>(smem);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int bh = blockIdx.x;
+  const int it_tile = gridDim.y - 1 - blockIdx.y;  // queries with the most causal keys first
+  const int q0 = 128 * it_tile;
+  int kend = A.valid;
+  if (A.causal && q0 + 128 < kend) kend = q0 + 128;
+  const int niter = (kend + 127) / 128;
+  const uint32_t tmem = setup<HD>(smem, b, &tm_q, &tm_g, &tm_k, &tm_v);
+
+  if (warp == C::kTmaWarp) {
+    if (lane == 0) produce<HD>(smem, b, &tm_q, &tm_g, &tm_k, &tm_v, q0, 0, niter, bh, A.status);
+  } else if (warp == C::kMmaWarp) {
+    if (lane == 0) issue<HD, false>(smem, b, tmem, niter, A.status);
+  } else {
+    const int g = warp >> 2, sub = warp & 3;
+    const int row = sub * 32 + lane;
+    const int qry = q0 + row;
+    const uint32_t lane_off = static_cast<uint32_t>(sub * 32) << 16;
+    const long long rbase = static_cast<long long>(bh) * A.L;
+    const bool in = qry < A.L;
+    const float inv = in ? 1.0f / A.dtot[rbase + qry] : 0.0f;
+    const float ev = in ? A.e[rbase + qry] : 0.0f;
+    bool ok = true;
+    for (int it = 0; ok && it < niter; ++it) {
+      const int kc0 = 128 * it + 32 * g;
+      ok = mbar_wait(b.s_full, it & 1, A.status, kDevTimeoutSoftmax);
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok) break;
+      tc_fence_after();
+      uint32_t x[32], y[32], wp[16], dp[16];
+      tmem_ld32(tmem + C::X_COL + lane_off + 32 * g, x);
+      tmem_ld32(tmem + C::Y_COL + lane_off + 32 * g, y);
+      tmem_ld_wait();
+      const bool need_mask = 128 * it + 127 >= A.valid || (A.causal && 128 * it + 127 > q0);
+      if (need_mask)
+        grad_chunk<true, false>(x, y, wp, dp, A.scale, nullptr, nullptr, inv, ev, A.valid, in, A.causal, qry, kc0,
+                                false);
+      else
+        grad_chunk<false, false>(x, y, wp, dp, A.scale, nullptr, nullptr, inv, ev, 0, true, 0, 0, 0, false);
+      // dS over the first half of the S columns: the A operand of dQ += dS K.
+      tmem_st16(tmem + C::X_COL + lane_off + 32 * g, dp);
+      tmem_st_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(b.g_full);
+    }
+    constexpr int OC = HD / 4;
+    bool have = niter > 0 && ok;
+    if (have) {
+      have = mbar_wait(b.o_full, 0, A.status, kDevTimeoutEpilogue);
+      have = __all_sync(0xffffffffu, have);
+    }
+    tc_fence_after();
+    uint32_t ov[32];
+    __syncwarp();
+    if (have) {
+      const uint32_t o_tm = tmem + C::ACC0 + lane_off + OC * g;
+      if constexpr (OC == 32) {
+        tmem_ld32(o_tm, ov);
+      } else {
+        uint32_t (&ov16)[16] = *reinterpret_cast<uint32_t(*)[16]>(ov);
+        tmem_ld16(o_tm, ov16);
+      }
+      tmem_ld_wait();
+    } else {
+#pragma unroll
+      for (int c = 0; c < 32; ++c) ov[c] = 0u;
+    }
+    if (in && (have || niter == 0)) {
+      __nv_bfloat16* dst = A.dq + (rbase + qry) * HD + OC * g;
+#pragma unroll
+      for (int w8 = 0; w8 < OC / 8; ++w8) {
+        uint4 pkt;
+        pkt.x = pack_bf16x2(__uint_as_float(ov[8 * w8 + 0]), __uint_as_float(ov[8 * w8 + 1]));
+        pkt.y = pack_bf16x2(__uint_as_float(ov[8 * w8 + 2]), __uint_as_float(ov[8 * w8 + 3]));
+        pkt.z = pack_bf16x2(__uint_as_float(ov[8 * w8 + 4]), __uint_as_float(ov[8 * w8 + 5]));
+        pkt.w = pack_bf16x2(__uint_as_float(ov[8 * w8 + 6]), __uint_as_float(ov[8 * w8 + 7]));
+        reinterpret_cast<uint4*>(dst)[w8] = pkt;
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == C::kMmaWarp) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem, C::TMEM_COLS);
+  }
+}
+
+template <int HD>
+cudaError_t launch_bwd_tc_hd(const void* q, const void* k, const void* v, const void* g, const BwdTcArgs& A, int bh,
+                             cudaStream_t stream, const char** detail) {
+  using C = BwdCfg<HD>;
+  static bool attr_set[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 64 && !attr_set[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(afa_bwd_dkv_tc_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         C::SMEM_BYTES);
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(afa_bwd_dq_tc_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               C::SMEM_BYTES);
+    if (e != cudaSuccess) {
+      *detail = "cudaFuncSetAttribute(max dynamic shared memory) failed";
+      return e;
+    }
+    attr_set[dev] = true;
+  }
+  CUtensorMap tq, tg, tk, tv;
+  if (!make_tmap(&tq, q, HD, A.L, bh) || !make_tmap(&tg, g, HD, A.L, bh) || !make_tmap(&tk, k, HD, A.L, bh) ||
+      !make_tmap(&tv, v, HD, A.L, bh)) {
+    *detail = "cuTensorMapEncodeTiled failed (pointers must be 16-byte aligned)";
+    return cudaErrorInvalidValue;
+  }
+  const int tiles = (A.L + 127) / 128;
+  afa_bwd_dkv_tc_kernel<HD><<<dim3(bh, tiles), C::kThreads, C::SMEM_BYTES, stream>>>(tq, tg, tk, tv, A);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  afa_bwd_dq_tc_kernel<HD><<<dim3(bh, tiles), C::kThreads, C::SMEM_BYTES, stream>>>(tq, tg, tk, tv, A);
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+bool tc_bwd_supported(int dtype, int d) { return dtype == kBF16 && (d == 64 || d == 128); }
+
+cudaError_t launch_tc_bwd(const void* q, const void* k, const void* v, const void* g_out, const float* d_total,
+                          const float* e, void* dq, void* dk, void* dv, int B, int H, int L, int D, int causal,
+                          int valid, float scale, int* status, cudaStream_t stream, const char** detail) {
+  BwdTcArgs A{};
+  A.dtot = d_total;
+  A.e = e;
+  A.dq = static_cast<__nv_bfloat16*>(dq);
+  A.dk = static_cast<__nv_bfloat16*>(dk);
+  A.dv = static_cast<__nv_bfloat16*>(dv);
+  A.status = status;
+  A.L = L;
+  A.causal = causal;
+  A.valid = valid;
+  A.scale = scale;
+  return D == 128 ? launch_bwd_tc_hd<128>(q, k, v, g_out, A, B * H, stream, detail)
+                  : launch_bwd_tc_hd<64>(q, k, v, g_out, A, B * H, stream, detail);
+}
+
+}  // namespace afa

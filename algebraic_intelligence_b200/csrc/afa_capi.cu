@@ -102,6 +102,7 @@ int set_last_error(int code, const char* msg) {
   g_last_error = msg;
   return code;
 }
+int* device_status_ptr() { return status_ptr(); }
 }  // namespace afa
 
 extern "C" {

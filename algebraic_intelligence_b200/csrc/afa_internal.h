@@ -40,6 +40,11 @@ bool tc_fwd_supported(int dtype, int d);
 cudaError_t launch_tc_fwd(Launch L, int dtype, cudaStream_t stream, const char** detail);
 cudaError_t launch_simt_fwd(Launch L, int dtype, cudaStream_t stream, const char** detail);
 
+bool tc_bwd_supported(int dtype, int d);
+cudaError_t launch_tc_bwd(const void* q, const void* k, const void* v, const void* g_out, const float* d_total,
+                          const float* e, void* dq, void* dk, void* dv, int B, int H, int L, int D, int causal,
+                          int valid, float scale, int* status, cudaStream_t stream, const char** detail);
+
 cudaError_t launch_finalize(const void* o_acc, const void* d_acc, void* out, void* dtot, long long rows, int d,
                             int dtype, double sink, cudaStream_t stream);
 
@@ -55,5 +60,8 @@ cudaError_t launch_octic(const void* x, void* y, long long n, int dtype, cudaStr
 
 // Records `msg` as the calling thread's afa_last_error() and returns `code`.
 int set_last_error(int code, const char* msg);
+
+// The calling device's status word (where bounded waits report), or nullptr.
+int* device_status_ptr();
 
 }  // namespace afa
