@@ -14,16 +14,19 @@
 //     tiles that see it. TMEM holds S^T = K Q^T and dP^T = V dO^T (keys on the
 //     lanes), then dV and dK. A thread owns one key (one TMEM lane); warpgroup g
 //     owns query columns [32g, 32g+32). It turns its S^T and dP^T columns into
-//     W^T and dS^T, written back as packed bf16 over the first half of the
-//     columns it read, which is the A operand layout of the next two MMAs:
+//     W^T and dS^T, written back as packed bf16 over its dP^T columns, which is
+//     the A operand layout of the next two MMAs:
 //     dV += W^T dO and dK += dS^T Q (B = the dO / Q tile read MN-major, the
 //     same shared-memory tile the S^T MMA read K-major).
 //   afa_bwd_dq_tc_kernel   one 128-query tile per CTA, looping over visible key
 //     tiles: S = Q K^T and dP = dO V^T, then dQ += dS K with dS from TMEM
 //     (queries on the lanes, per-row 1/d_total and E in registers).
 //
-// TMEM columns: X (S^T or S) [0,128), Y (dP^T or dP) [128,256), accumulators
-// from 256. K/Q/V/dO tiles are TMA-loaded with 128-byte swizzle, no multicast.
+// TMEM columns: X (S^T or S) [0,128), then one or two Y buffers (dP^T or dP,
+// then the packed dS and W), then the accumulators (struct Tmem). The next
+// tile's S (and, with two Y buffers, its dP) runs on the tensor core while the
+// grad warps work on this tile. K/Q/V/dO tiles are TMA-loaded with 128-byte
+// swizzle, no multicast.
 // Every wait is bounded (afa_common.cuh) and reports to the device status word.
 #include <cstdio>
 
@@ -48,13 +51,25 @@ struct BwdCfg {
   static constexpr int ST_OFF = 2 * TILE_BYTES;
   static constexpr int VEC_OFF = ST_OFF + NST * 2 * TILE_BYTES;  // per grad warp: 32 x (1/d, E) floats
   static constexpr int BAR_OFF = VEC_OFF + 16 * 64 * 4;
-  static constexpr int NBAR = 1 + 2 * NST + 4;  // fix_full, st_full[], st_empty[], s_full, g_full, o_full, drain
+  static constexpr int NBAR = 1 + 2 * NST + 6;  // fix_full, st_full[], st_empty[], s_full, x_read, g_full[2], o_full, drain
   static constexpr int SMEM_BYTES = BAR_OFF + NBAR * 8 + 16 + 1024;
   static constexpr uint32_t TMEM_COLS = 512;
-  static constexpr uint32_t X_COL = 0, Y_COL = 128, ACC0 = 256, ACC1 = 256 + HD;
+  static constexpr uint32_t X_COL = 0;
   __device__ static constexpr uint32_t p_col(int kk) {
     return static_cast<uint32_t>((kk >> 1) * 32 + (kk & 1) * 8);
   }
+};
+
+// TMEM columns. X holds S (or S^T); Y holds dP (or dP^T) and then, packed as
+// bf16 over each 32-column chunk, dS in the first 16 columns and W in the
+// last 16 (the A operands of the accumulating products). With DBY there are
+// two Y buffers, so the next tile's S and dP run while this tile's grad math
+// does; without, only the next S does. Accumulators follow.
+template <int HD, bool DBY>
+struct Tmem {
+  __device__ static constexpr uint32_t y(int b) { return 128u + (DBY ? 128u * static_cast<uint32_t>(b) : 0u); }
+  static constexpr uint32_t ACC0 = DBY ? 384u : 256u;
+  static constexpr uint32_t ACC1 = ACC0 + HD;
 };
 
 struct BwdTcArgs {
@@ -69,7 +84,7 @@ struct BwdTcArgs {
 };
 
 struct Bars {
-  uint64_t *fix_full, *st_full, *st_empty, *s_full, *g_full, *o_full, *drain;
+  uint64_t *fix_full, *st_full, *st_empty, *s_full, *x_read, *g_full, *o_full, *drain;
   uint32_t* tmem_slot;
 };
 
@@ -82,8 +97,9 @@ __device__ __forceinline__ Bars carve(uint8_t* smem) {
   b.st_full = bars + 1;
   b.st_empty = b.st_full + C::NST;
   b.s_full = b.st_empty + C::NST;
-  b.g_full = b.s_full + 1;
-  b.o_full = b.g_full + 1;
+  b.x_read = b.s_full + 1;
+  b.g_full = b.x_read + 1;  // two, by tile parity (see issue())
+  b.o_full = b.g_full + 2;
   b.drain = b.o_full + 1;
   b.tmem_slot = reinterpret_cast<uint32_t*>(b.drain + 1);
   return b;
@@ -101,7 +117,9 @@ __device__ __forceinline__ uint32_t setup(uint8_t* smem, const Bars& b, const CU
       mbar_init(b.st_empty + s, 1);
     }
     mbar_init(b.s_full, 1);
-    mbar_init(b.g_full, 16);  // one elected arrive per grad warp
+    mbar_init(b.x_read, 16);  // one elected arrive per grad warp
+    mbar_init(b.g_full, 16);
+    mbar_init(b.g_full + 1, 16);
     mbar_init(b.o_full, 1);
     mbar_init(b.drain, 1);
     fence_barrier_init();
@@ -152,54 +170,88 @@ __device__ __forceinline__ void produce(uint8_t* smem, const Bars& b, const CUte
     (void)mbar_wait(b.st_full + (it % C::NST), (it / C::NST) & 1, nullptr, 0);
 }
 
-// MMA issuer. Per iteration: X = F0 S0^T and Y = F1 S1^T (F = fixed tiles,
-// S = streamed tiles, both K-major), then, once the grad warps have written
-// the packed bf16 operands, ACC0 += X' M0 and (if two products) ACC1 += Y' M1,
-// where M0/M1 are streamed tiles read MN-major.
-//   dK/dV kernel: F = (K, V), S = (Q, dO): ACC0 = dV += W^T dO, ACC1 = dK += dS^T Q.
-//   dQ kernel:    F = (Q, dO), S = (K, V): ACC0 = dQ += dS K (one product).
-template <int HD, bool TWO>
+// MMA issuer. X = F0 S0^T and Y = F1 S1^T (F = the CTA's fixed tiles, S =
+// the streamed pair, both read K-major); once the grad warps have written the
+// packed operands into Y, the accumulating products read the streamed tiles
+// MN-major:
+//   dK/dV kernel (TWO): F = (K, V), S = (Q, dO); ACC0 = dV += W^T dO,
+//                       ACC1 = dK += dS^T Q.
+//   dQ kernel:          F = (Q, dO), S = (K, V); ACC0 = dQ += dS K.
+// Order per tile j: [wait the grad warps' reads of X] next X (and next Y with
+// DBY), [wait the packed operands] this tile's products, release the stage,
+// next Y (without DBY). With DBY the grad warps may finish tile j+1 before
+// this thread has seen tile j's operands ready, so that signal alternates
+// between two barriers: reaching tile j+2 needs an s_full committed only after
+// this thread passed tile j's wait, so no barrier gets two phases ahead.
+template <int HD, bool TWO, bool DBY>
 __device__ __forceinline__ void issue(uint8_t* smem, const Bars& b, uint32_t tmem, int niter, int* status) {
   using C = BwdCfg<HD>;
+  using T = Tmem<HD, DBY>;
   if (niter <= 0) return;
   constexpr uint32_t idesc_x = idesc_bf16_f32(128, 128, false);
   constexpr uint32_t idesc_acc = idesc_bf16_f32(128, HD, true);
   const uint32_t fix = smem_u32(smem + C::FIX_OFF);
-  bool ok = mbar_wait(b.fix_full, 0, status, kDevTimeoutMma);
-  for (int it = 0; ok && it < niter; ++it) {
-    const int s = it % C::NST;
-    if (!(ok = mbar_wait(b.st_full + s, (it / C::NST) & 1, status, kDevTimeoutMma))) break;
+  auto stage = [&](int j) { return smem_u32(smem + C::ST_OFF + (j % C::NST) * 2 * C::TILE_BYTES); };
+  auto score = [&](int t, int j, uint32_t dst) {  // t = 0: X = F0 S0^T, t = 1: Y = F1 S1^T
+    const uint32_t st = stage(j);
+#pragma unroll
+    for (int kk = 0; kk < HD / 16; ++kk) {
+      const uint32_t off = (kk >> 2) * C::SUB_BYTES + (kk & 3) * 32;
+      const uint64_t a = sw128_desc(fix + t * C::TILE_BYTES + off, 16, 1024);
+      const uint64_t bd = sw128_desc(st + t * C::TILE_BYTES + off, 16, 1024);
+      umma_ss(tmem + dst, a, bd, idesc_x, kk > 0 ? 1u : 0u);
+    }
+  };
+  bool ok = mbar_wait(b.fix_full, 0, status, kDevTimeoutMma) && mbar_wait(b.st_full, 0, status, kDevTimeoutMma);
+  if (ok) {
     tc_fence_after();
-    const uint32_t st = smem_u32(smem + C::ST_OFF + s * 2 * C::TILE_BYTES);
-#pragma unroll
-    for (int t = 0; t < 2; ++t) {
-#pragma unroll
-      for (int kk = 0; kk < HD / 16; ++kk) {
-        const uint32_t off = (kk >> 2) * C::SUB_BYTES + (kk & 3) * 32;
-        const uint64_t a = sw128_desc(fix + t * C::TILE_BYTES + off, 16, 1024);
-        const uint64_t bd = sw128_desc(st + t * C::TILE_BYTES + off, 16, 1024);
-        umma_ss(tmem + (t ? C::Y_COL : C::X_COL), a, bd, idesc_x, kk > 0 ? 1u : 0u);
+    score(0, 0, C::X_COL);
+    score(1, 0, T::y(0));
+    umma_commit(b.s_full);
+  }
+  for (int j = 0; ok && j < niter; ++j) {
+    const int yb = DBY ? (j & 1) : 0;
+    const bool more = j + 1 < niter;
+    if (!(ok = mbar_wait(b.x_read, j & 1, status, kDevTimeoutMma))) break;
+    if (more) {
+      const int sn = (j + 1) % C::NST;
+      if (!(ok = mbar_wait(b.st_full + sn, ((j + 1) / C::NST) & 1, status, kDevTimeoutMma))) break;
+      tc_fence_after();
+      score(0, j + 1, C::X_COL);
+      if constexpr (DBY) {
+        score(1, j + 1, T::y((j + 1) & 1));
+        umma_commit(b.s_full);
       }
     }
-    umma_commit(b.s_full);
-    if (!(ok = mbar_wait(b.g_full, it & 1, status, kDevTimeoutMma))) break;
+    if (!(ok = mbar_wait(b.g_full + (j & 1), (j >> 1) & 1, status, kDevTimeoutMma))) break;
     tc_fence_after();
-    // dK/dV: ACC0 (dV) from X' = W^T against dO (the second streamed tile),
-    // ACC1 (dK) from Y' = dS^T against Q (the first). dQ: ACC0 from X' = dS
-    // against K (the first streamed tile).
-#pragma unroll
-    for (int kk = 0; kk < 8; ++kk) {
-      const uint64_t m0 = sw128_desc(st + (TWO ? C::TILE_BYTES : 0) + kk * 2048, C::SUB_BYTES, 1024);
-      umma_ts(tmem + C::ACC0, tmem + C::X_COL + C::p_col(kk), m0, idesc_acc, (it > 0 || kk > 0) ? 1u : 0u);
-    }
+    const uint32_t st = stage(j);
+    const uint32_t ya = T::y(yb);
     if constexpr (TWO) {
 #pragma unroll
-      for (int kk = 0; kk < 8; ++kk) {
-        const uint64_t m1 = sw128_desc(st + kk * 2048, C::SUB_BYTES, 1024);
-        umma_ts(tmem + C::ACC1, tmem + C::Y_COL + C::p_col(kk), m1, idesc_acc, (it > 0 || kk > 0) ? 1u : 0u);
+      for (int kk = 0; kk < 8; ++kk) {  // dV += W^T dO
+        const uint64_t m = sw128_desc(st + C::TILE_BYTES + kk * 2048, C::SUB_BYTES, 1024);
+        umma_ts(tmem + T::ACC0, tmem + ya + C::p_col(kk) + 16, m, idesc_acc, (j > 0 || kk > 0) ? 1u : 0u);
+      }
+#pragma unroll
+      for (int kk = 0; kk < 8; ++kk) {  // dK += dS^T Q
+        const uint64_t m = sw128_desc(st + kk * 2048, C::SUB_BYTES, 1024);
+        umma_ts(tmem + T::ACC1, tmem + ya + C::p_col(kk), m, idesc_acc, (j > 0 || kk > 0) ? 1u : 0u);
+      }
+    } else {
+#pragma unroll
+      for (int kk = 0; kk < 8; ++kk) {  // dQ += dS K
+        const uint64_t m = sw128_desc(st + kk * 2048, C::SUB_BYTES, 1024);
+        umma_ts(tmem + T::ACC0, tmem + ya + C::p_col(kk), m, idesc_acc, (j > 0 || kk > 0) ? 1u : 0u);
       }
     }
-    umma_commit(b.st_empty + s);
+    umma_commit(b.st_empty + (j % C::NST));
+    if constexpr (!DBY) {
+      if (more) {  // Y is single: after this tile's products have read it
+        score(1, j + 1, T::y(0));
+        umma_commit(b.s_full);
+      }
+    }
   }
   if (ok) umma_commit(b.o_full);
   // Every MMA this thread issued must finish before TMEM is released.
@@ -209,42 +261,44 @@ __device__ __forceinline__ void issue(uint8_t* smem, const Bars& b, uint32_t tme
 
 // One 32-column chunk: scores x (raw S or S^T accumulator words), score
 // gradients y (dP or dP^T); per-column (dK/dV kernel) or per-row (dQ kernel)
-// 1/d_total and E. Writes packed bf16 W (if want_w) and dS.
+// 1/d_total and E. Writes packed bf16 W and dS. Element pairs go through the
+// packed fp32x2 instructions (FFMA2 / FMUL2), which halve the issue slots of
+// the map; the one MUFU op per element is the rsqrt.
 template <bool MASK, bool PER_COL>
 __device__ __forceinline__ void grad_chunk(const uint32_t (&x)[32], const uint32_t (&y)[32], uint32_t (&wp)[16],
                                            uint32_t (&dp)[16], float scale, const float* inv_c, const float* e_c,
                                            float inv_r, float e_r, int vis_lim, bool vis_row, int causal,
                                            int row_pos, int col_pos0, bool row_is_key) {
-  const float c8 = 8.0f * scale;
+  const float2 sc = make_float2(scale, scale);
+  const float2 c8 = make_float2(8.0f * scale, 8.0f * scale);
+  const float2 one = make_float2(1.0f, 1.0f);
 #pragma unroll
   for (int c = 0; c < 32; c += 2) {
-    float wv[2], dv[2];
-#pragma unroll
-    for (int u = 0; u < 2; ++u) {
-      const float s = __uint_as_float(x[c + u]) * scale;
-      const float rad = fmaf(s, s, 1.0f);
-      const float r = rsqrt_approx(rad);
-      const float rho = fmaf(rad, r, s);
-      const float p2 = rho * rho;
-      const float p4 = p2 * p2;
-      const float inv = PER_COL ? inv_c[c + u] : inv_r;
-      const float ev = PER_COL ? e_c[c + u] : e_r;
-      float w = p4 * p4 * inv;
-      float ds = c8 * (r * w) * (__uint_as_float(y[c + u]) - ev);
-      if (MASK) {
-        const int col = col_pos0 + c + u;
-        // row_is_key: the row is a key, the column a query; otherwise the reverse.
-        const int key = row_is_key ? row_pos : col;
-        const int qry = row_is_key ? col : row_pos;
-        const bool vis = vis_row && key < vis_lim && (!causal || key <= qry);
-        w = vis ? w : 0.0f;
-        ds = vis ? ds : 0.0f;
-      }
-      wv[u] = w;
-      dv[u] = ds;
+    const float2 s = __fmul2_rn(make_float2(__uint_as_float(x[c]), __uint_as_float(x[c + 1])), sc);
+    const float2 rad = __ffma2_rn(s, s, one);
+    const float2 r = make_float2(rsqrt_approx(rad.x), rsqrt_approx(rad.y));
+    const float2 rho = __ffma2_rn(rad, r, s);
+    const float2 p2 = __fmul2_rn(rho, rho);
+    const float2 p4 = __fmul2_rn(p2, p2);
+    const float2 inv = PER_COL ? make_float2(inv_c[c], inv_c[c + 1]) : make_float2(inv_r, inv_r);
+    const float2 ne = PER_COL ? make_float2(-e_c[c], -e_c[c + 1]) : make_float2(-e_r, -e_r);
+    float2 w = __fmul2_rn(__fmul2_rn(p4, p4), inv);
+    const float2 t = __fadd2_rn(make_float2(__uint_as_float(y[c]), __uint_as_float(y[c + 1])), ne);
+    float2 ds = __fmul2_rn(__fmul2_rn(r, w), __fmul2_rn(t, c8));
+    if (MASK) {
+      // row_is_key: the row is a key, the columns queries; otherwise the reverse.
+      const int col = col_pos0 + c;
+      const int key0 = row_is_key ? row_pos : col, key1 = row_is_key ? row_pos : col + 1;
+      const int qry0 = row_is_key ? col : row_pos, qry1 = row_is_key ? col + 1 : row_pos;
+      const bool v0 = vis_row && key0 < vis_lim && (!causal || key0 <= qry0);
+      const bool v1 = vis_row && key1 < vis_lim && (!causal || key1 <= qry1);
+      w.x = v0 ? w.x : 0.0f;
+      w.y = v1 ? w.y : 0.0f;
+      ds.x = v0 ? ds.x : 0.0f;
+      ds.y = v1 ? ds.y : 0.0f;
     }
-    wp[c >> 1] = pack_bf16x2(wv[0], wv[1]);
-    dp[c >> 1] = pack_bf16x2(dv[0], dv[1]);
+    wp[c >> 1] = pack_bf16x2(w.x, w.y);
+    dp[c >> 1] = pack_bf16x2(ds.x, ds.y);
   }
 }
 
@@ -265,10 +319,13 @@ __global__ void __launch_bounds__(576, 1)
   const int niter = k0 >= A.valid ? 0 : nq - i_first;
   const uint32_t tmem = setup<HD>(smem, b, &tm_q, &tm_g, &tm_k, &tm_v);
 
+  constexpr bool DBY = HD == 64;  // two dP^T buffers fit next to dV and dK only at head_dim 64
+  using T = Tmem<HD, DBY>;
+  static_assert(T::ACC1 + HD <= C::TMEM_COLS, "TMEM budget");
   if (warp == C::kTmaWarp) {
     if (lane == 0) produce<HD>(smem, b, &tm_k, &tm_v, &tm_q, &tm_g, k0, 128 * i_first, niter, bh, A.status);
   } else if (warp == C::kMmaWarp) {
-    if (lane == 0) issue<HD, true>(smem, b, tmem, niter, A.status);
+    if (lane == 0) issue<HD, true, DBY>(smem, b, tmem, niter, A.status);
   } else {
     const int g = warp >> 2, sub = warp & 3;
     const int row = sub * 32 + lane;
@@ -287,14 +344,19 @@ __global__ void __launch_bounds__(576, 1)
         vec[32 + lane] = in ? A.e[rbase + qi] : 0.0f;
         __syncwarp();
       }
+      const uint32_t yb = T::y(DBY ? (it & 1) : 0) + lane_off + 32 * g;
       ok = mbar_wait(b.s_full, it & 1, A.status, kDevTimeoutSoftmax);
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) break;
       tc_fence_after();
       uint32_t x[32], y[32], wp[16], dp[16];
       tmem_ld32(tmem + C::X_COL + lane_off + 32 * g, x);
-      tmem_ld32(tmem + C::Y_COL + lane_off + 32 * g, y);
+      tmem_ld32(tmem + yb, y);
       tmem_ld_wait();
+      // Scores are in registers: the next tile's S may overwrite X.
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(b.x_read);
       const bool need_mask = k0 + 127 >= A.valid || q0 + 127 >= A.L || (A.causal && q0 < k0 + 127);
       // Columns past L read 1/d = 0, which zeroes W and dS; the mask covers
       // invisible keys and causal order.
@@ -303,12 +365,12 @@ __global__ void __launch_bounds__(576, 1)
                                qc0, true);
       else
         grad_chunk<false, true>(x, y, wp, dp, A.scale, vec, vec + 32, 0.f, 0.f, 0, true, 0, 0, 0, true);
-      tmem_st16(tmem + C::X_COL + lane_off + 32 * g, wp);
-      tmem_st16(tmem + C::Y_COL + lane_off + 32 * g, dp);
+      tmem_st16(tmem + yb, dp);       // dS^T over the chunk's first 16 columns
+      tmem_st16(tmem + yb + 16, wp);  // W^T over its last 16
       tmem_st_wait();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(b.g_full);
+      if (lane == 0) mbar_arrive(b.g_full + (it & 1));
     }
     // Epilogue: warpgroup g stores columns [HD/4 g, HD/4 (g+1)) of dV and dK.
     constexpr int OC = HD / 4;
@@ -323,7 +385,7 @@ __global__ void __launch_bounds__(576, 1)
       uint32_t ov[32];
       __syncwarp();
       if (have) {
-        const uint32_t o_tm = tmem + (t ? C::ACC1 : C::ACC0) + lane_off + OC * g;
+        const uint32_t o_tm = tmem + (t ? T::ACC1 : T::ACC0) + lane_off + OC * g;
         if constexpr (OC == 32) {
           tmem_ld32(o_tm, ov);
         } else {
@@ -377,10 +439,12 @@ __global__ void __launch_bounds__(576, 1)
   const int niter = (kend + 127) / 128;
   const uint32_t tmem = setup<HD>(smem, b, &tm_q, &tm_g, &tm_k, &tm_v);
 
+  using T = Tmem<HD, true>;
+  static_assert(T::ACC0 + HD <= C::TMEM_COLS, "TMEM budget");
   if (warp == C::kTmaWarp) {
     if (lane == 0) produce<HD>(smem, b, &tm_q, &tm_g, &tm_k, &tm_v, q0, 0, niter, bh, A.status);
   } else if (warp == C::kMmaWarp) {
-    if (lane == 0) issue<HD, false>(smem, b, tmem, niter, A.status);
+    if (lane == 0) issue<HD, false, true>(smem, b, tmem, niter, A.status);
   } else {
     const int g = warp >> 2, sub = warp & 3;
     const int row = sub * 32 + lane;
@@ -393,26 +457,31 @@ __global__ void __launch_bounds__(576, 1)
     bool ok = true;
     for (int it = 0; ok && it < niter; ++it) {
       const int kc0 = 128 * it + 32 * g;
+      const uint32_t yb = T::y(it & 1) + lane_off + 32 * g;
       ok = mbar_wait(b.s_full, it & 1, A.status, kDevTimeoutSoftmax);
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) break;
       tc_fence_after();
       uint32_t x[32], y[32], wp[16], dp[16];
       tmem_ld32(tmem + C::X_COL + lane_off + 32 * g, x);
-      tmem_ld32(tmem + C::Y_COL + lane_off + 32 * g, y);
+      tmem_ld32(tmem + yb, y);
       tmem_ld_wait();
+      // Scores are in registers: the next tile's S may overwrite X.
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(b.x_read);
       const bool need_mask = 128 * it + 127 >= A.valid || (A.causal && 128 * it + 127 > q0);
       if (need_mask)
         grad_chunk<true, false>(x, y, wp, dp, A.scale, nullptr, nullptr, inv, ev, A.valid, in, A.causal, qry, kc0,
                                 false);
       else
         grad_chunk<false, false>(x, y, wp, dp, A.scale, nullptr, nullptr, inv, ev, 0, true, 0, 0, 0, false);
-      // dS over the first half of the S columns: the A operand of dQ += dS K.
-      tmem_st16(tmem + C::X_COL + lane_off + 32 * g, dp);
+      // dS over the chunk's first 16 dP columns: the A operand of dQ += dS K.
+      tmem_st16(tmem + yb, dp);
       tmem_st_wait();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(b.g_full);
+      if (lane == 0) mbar_arrive(b.g_full + (it & 1));
     }
     constexpr int OC = HD / 4;
     bool have = niter > 0 && ok;
@@ -424,7 +493,7 @@ __global__ void __launch_bounds__(576, 1)
     uint32_t ov[32];
     __syncwarp();
     if (have) {
-      const uint32_t o_tm = tmem + C::ACC0 + lane_off + OC * g;
+      const uint32_t o_tm = tmem + T::ACC0 + lane_off + OC * g;
       if constexpr (OC == 32) {
         tmem_ld32(o_tm, ov);
       } else {

@@ -16,7 +16,8 @@ the largest single-GPU configuration of BASELINE.json.
 
 At N=1 the line also carries the other BASELINE configurations measured in the
 same run (``sub``): config 3 (prefill L=4096, the 60%-of-peak target), config 2
-(prefill L=2048 with K outliers) and config 4 (decode, HBM GB/s).
+(prefill L=2048 with K outliers), config 4 (decode, HBM GB/s) and the backward
+of config 3.
 
 ``--impl reference`` times the reference's CPU implementation of the path (the
 float64 NumPy oracle of tests/reference_attention.py, restated in
@@ -376,6 +377,38 @@ def run_prefill(cfg, args, peaks, outliers=False):
                          "frac": ach / peaks["bf16_tflops"], "peak_source": peaks["source"] + " bf16_tflops"}}
 
 
+def run_backward(cfg, args, peaks):
+    """Backward of a prefill configuration (tiled_afa_backward): dq, dk, dv
+    from q, k, v, the forward's out and d_total, and g_out. FLOPs count the
+    five products of pallas_afa.py:500-510 over causal pairs, 10*B*H*D per pair
+    (2.5x the forward); the kernels also recompute S and dP, which is not
+    counted."""
+    import torch
+    import algebraic_intelligence_b200 as afa
+    B, H, L, D = cfg["B"], cfg["H"], cfg["L"], cfg["D"]
+    sets = []
+    for seed in (0, 1):
+        gen = torch.Generator(device="cuda").manual_seed(seed)
+        q, k, v, g = (randn_bf16((B, H, L, D), gen) for _ in range(4))
+        out, den = afa.pallas_afa_forward(q, k, v, causal=True, return_denominator=True)
+        sets.append((q, k, v, out, den, g))
+    flops = 2.5 * causal_flops(**cfg)
+
+    def step(i, kt):
+        q, k, v, out, den, g = sets[i % 2]
+        f = lambda: afa.tiled_afa_backward(q, k, v, out, den, g, causal=True)  # noqa: E731
+        kt.around(f) if kt else f()
+
+    steps = max(args.steps, 10)
+    ms, kt = timed(step, steps, max(args.warmup, 3), 1)
+    kms = kt.mean_ms()
+    ach = flops / (kms / 1e3) / 1e12
+    return {"value": flops * steps / (ms / 1e3) / 1e12, "unit": UNIT, "ms_per_step": ms / steps,
+            "flops": flops, "kernels_per_step": 3,
+            "roofline": {"bound": "tensor", "achieved": ach, "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
+                         "frac": ach / peaks["bf16_tflops"], "peak_source": peaks["source"] + " bf16_tflops"}}
+
+
 def run_decode(args, peaks, cfg=DEC):
     import torch
     import algebraic_intelligence_b200 as afa
@@ -484,7 +517,8 @@ def main():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="all", choices=["all", "ring", "ring8_hop", "prefill3", "prefill2", "decode", "decode_small"],
+    ap.add_argument("--workload", default="all", choices=["all", "ring", "ring8_hop", "prefill3", "prefill2", "backward3", "decode",
+                                                      "decode_small"],
                     help="profiling aid: run one workload only (N=1)")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     args = ap.parse_args()
@@ -506,6 +540,7 @@ def main():
               "ring8_hop": lambda: run_ring_hop(args, peaks),
               "prefill3": lambda: run_prefill(CFG3, args, peaks),
               "prefill2": lambda: run_prefill(CFG2, args, peaks, outliers=True),
+              "backward3": lambda: run_backward(CFG3, args, peaks),
               "decode": lambda: run_decode(args, peaks),
               "decode_small": lambda: run_decode(args, peaks, DEC_SMALL)}[args.workload]
         res = fn()
@@ -524,6 +559,7 @@ def main():
         sub["prefill_config3_L4096"] = run_prefill(CFG3, args, peaks)
         sub["prefill_config2_L2048_outliers"] = run_prefill(CFG2, args, peaks, outliers=True)
         sub["decode_config4"] = run_decode(args, peaks)
+        sub["backward_config3_L4096"] = run_backward(CFG3, args, peaks)
     status = _lib.device_status(torch.device("cuda", local))
     if rank == 0:
         line = {
