@@ -30,6 +30,9 @@ SIGNATURES = {
     "afa_finalize": (_c_int, [_c_void_p] * 4 + [_c_ll, _c_int, _c_int, _c_float, _c_void_p]),
     "afa_bwd": (_c_int, [_c_void_p] * 9 + [_c_int] * 7 + [_c_void_p, _c_size, _c_void_p]),
     "afa_bwd_workspace_bytes": (_c_size, [_c_int] * 5),
+    "afa_ago_table": (_c_int, [_c_void_p, _c_void_p, _c_int, _c_int, ctypes.POINTER(_c_double), _c_double, _c_int,
+                               _c_void_p]),
+    "afa_ago_rotate": (_c_int, [_c_void_p] * 6 + [_c_int, _c_ll, _c_int, _c_int, _c_ll, _c_int, _c_void_p]),
     "afa_ring_export": (_c_int, [_c_void_p, _c_void_p, ctypes.POINTER(ctypes.c_ulonglong)]),
     "afa_ring_open": (_c_int, [_c_void_p, ctypes.POINTER(_c_void_p)]),
     "afa_ring_close": (_c_int, [_c_void_p]),

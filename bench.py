@@ -16,8 +16,8 @@ the largest single-GPU configuration of BASELINE.json.
 
 At N=1 the line also carries the other BASELINE configurations measured in the
 same run (``sub``): config 3 (prefill L=4096, the 60%-of-peak target), config 2
-(prefill L=2048 with K outliers), config 4 (decode, HBM GB/s) and the backward
-of config 3.
+(prefill L=2048 with K outliers), config 4 (decode, HBM GB/s), the backward
+of config 3 and the AGO Q/K rotation at config 3's shape (HBM GB/s).
 
 ``--impl reference`` times the reference's CPU implementation of the path (the
 float64 NumPy oracle of tests/reference_attention.py, restated in
@@ -409,6 +409,35 @@ def run_backward(cfg, args, peaks):
                          "frac": ach / peaks["bf16_tflops"], "peak_source": peaks["source"] + " bf16_tflops"}}
 
 
+def run_ago(cfg, args, peaks):
+    """AGO rotation of Q and K (apply_ago_rotations, the attention layer's Q/K
+    prologue) at a prefill configuration's shape, bf16 with float32 tables:
+    HBM-bound, bytes = read + write of both tensors."""
+    import torch
+    import algebraic_intelligence_b200 as afa
+    B, H, L, D = cfg["B"], cfg["H"], cfg["L"], cfg["D"]
+    rot = afa.build_cayley_rotary_matrix(D, L, dtype=torch.float32)
+    sets = []
+    for seed in (0, 1):
+        gen = torch.Generator(device="cuda").manual_seed(seed)
+        sets.append(tuple(randn_bf16((B, H, L, D), gen) for _ in range(2)))
+    nbytes = 4.0 * B * H * L * D * 2
+
+    def step(i, kt):
+        q, k = sets[i % 2]
+        f = lambda: afa.apply_ago_rotations(q, k, rotary_params=rot, seq_axis=2)  # noqa: E731
+        kt.around(f) if kt else f()
+
+    steps = max(args.steps, 10)
+    ms, kt = timed(step, steps, max(args.warmup, 3), 1)
+    kms = kt.mean_ms()
+    ach = nbytes / (kms / 1e3) / 1e9
+    return {"value": nbytes * steps / (ms / 1e3) / 1e9, "unit": "GB/s", "ms_per_step": ms / steps,
+            "bytes": nbytes,
+            "roofline": {"bound": "hbm", "achieved": ach, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                         "frac": ach / peaks["hbm_gbs"], "peak_source": peaks["source"] + " hbm_gbs"}}
+
+
 def run_decode(args, peaks, cfg=DEC):
     import torch
     import algebraic_intelligence_b200 as afa
@@ -517,8 +546,8 @@ def main():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="all", choices=["all", "ring", "ring8_hop", "prefill3", "prefill2", "backward3", "decode",
-                                                      "decode_small"],
+    ap.add_argument("--workload", default="all", choices=["all", "ring", "ring8_hop", "prefill3", "prefill2", "backward3", "ago3",
+                                                      "decode", "decode_small"],
                     help="profiling aid: run one workload only (N=1)")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     args = ap.parse_args()
@@ -541,6 +570,7 @@ def main():
               "prefill3": lambda: run_prefill(CFG3, args, peaks),
               "prefill2": lambda: run_prefill(CFG2, args, peaks, outliers=True),
               "backward3": lambda: run_backward(CFG3, args, peaks),
+              "ago3": lambda: run_ago(CFG3, args, peaks),
               "decode": lambda: run_decode(args, peaks),
               "decode_small": lambda: run_decode(args, peaks, DEC_SMALL)}[args.workload]
         res = fn()
@@ -560,6 +590,7 @@ def main():
         sub["prefill_config2_L2048_outliers"] = run_prefill(CFG2, args, peaks, outliers=True)
         sub["decode_config4"] = run_decode(args, peaks)
         sub["backward_config3_L4096"] = run_backward(CFG3, args, peaks)
+        sub["ago_rotate_config3_shape"] = run_ago(CFG3, args, peaks)
     status = _lib.device_status(torch.device("cuda", local))
     if rank == 0:
         line = {

@@ -17,6 +17,8 @@
  *                            (pallas_afa.py:651-652)
  *   afa_bwd               <- tiled_afa_backward (pallas_afa.py:409-522), the VJP
  *                            of pallas_afa (:555-615)
+ *   afa_ago_table         <- build_cayley_rotary_matrix (src/attention.py:156-207)
+ *   afa_ago_rotate        <- apply_ago_rotations (src/attention.py:210-240)
  *   afa_decode            <- no reference counterpart: exact AFA for one query
  *                            token over a KV cache (pallas_afa_forward with Lq=1)
  *   algebraic_softmax_fwd <- algebraic_softmax   (src/attention.py:88-91, :59-67)
@@ -167,6 +169,28 @@ AFA_API int afa_bwd(const void* q, const void* k, const void* v, const void* out
                     const void* g_out, void* dq, void* dk, void* dv, int B, int H, int L, int D, int dtype,
                     int causal, int valid_len, void* workspace, size_t workspace_bytes, void* stream);
 AFA_API size_t afa_bwd_workspace_bytes(int B, int H, int L, int D, int dtype);
+
+/*
+ * AGO rotary position rotations, the Q/K prologue of the attention layer
+ * (src/model.py:262-264).
+ *   afa_ago_table   build_cayley_rotary_matrix (src/attention.py:156-207):
+ *                   c, s = (max_seq_len, dim/2) tables in `dtype`, computed in
+ *                   float32 (float64 for AFA_F64). freqs: optional HOST array of
+ *                   dim/2 doubles (the explicit rational frequencies); NULL uses
+ *                   the default ladder from `base`. dim even, at most 512.
+ *   afa_ago_rotate  apply_ago_rotations (src/attention.py:210-240): rotates q and
+ *                   k (contiguous, same shape, last axis = dim) into q_out and k_out
+ *                   (which may alias them). Row r (of rows = elements / dim) sits
+ *                   at sequence position (r / inner) % seq_len; inner is the
+ *                   product of the axes between the sequence axis and the last.
+ *                   c, s: (>= seq_len, dim/2) tables in table_dtype, cast to
+ *                   `dtype` before use as in the reference.
+ */
+AFA_API int afa_ago_table(void* c, void* s, int dim, int max_seq_len, const double* freqs, double base, int dtype,
+                          void* stream);
+AFA_API int afa_ago_rotate(const void* q, const void* k, void* q_out, void* k_out, const void* c, const void* s,
+                           int table_dtype, long long rows, int dim, int seq_len, long long inner, int dtype,
+                           void* stream);
 
 /*
  * Decode step (no reference counterpart; the math of pallas_afa_forward with a

@@ -33,6 +33,14 @@ It restates, in float64 NumPy, the reference's own ground truth
 * ``decode``           -- exact AFA for one query token over a KV cache; the
                           reference has no decode kernel, so its oracle is
                           ``afa`` with Lq = 1, non-causal.
+* ``cayley_tables``    -- the AGO rotary tables (c, s) of
+                          tests/reference_ago.py:21-53 (the float64 oracle of
+                          build_cayley_rotary_matrix, src/attention.py:156-207):
+                          rational Cayley frequencies and a renormalised
+                          rotation recurrence over positions.
+* ``ago_rotate``       -- apply_ago_rotations (tests/reference_ago.py:56-94,
+                          src/attention.py:210-240): each channel pair (x0, x1)
+                          at position m becomes (c x0 - s x1, s x0 + c x1).
 * ``afa_backward``     -- gradients of sum(afa(q, k, v) * g_out) by the
                           analytical single-pass backward of
                           src/kernels/pallas_afa.py:409-522
@@ -62,6 +70,9 @@ __all__ = [
     "zigzag_chunks",
     "decode",
     "afa_backward",
+    "cayley_tables",
+    "ago_rotate",
+    "ago_seq_axis",
     "rel_err",
 ]
 
@@ -213,6 +224,71 @@ def afa_backward(q, k, v, g_out, sink=0.5, causal=False, valid_len=None, block=5
         dk += np.matmul(np.swapaxes(ds, -1, -2), qb)
         dv += np.matmul(np.swapaxes(w, -1, -2), gb)
     return dq, dk, dv
+
+
+def cayley_tables(dim, max_seq_len, freqs=None, base=10000.0):
+    """(c, s), each (max_seq_len, dim // 2), float64 (reference_ago.py:21-53).
+
+    w_k = 1 / (1 + alpha k)^2 with alpha = (sqrt(base) - 1) / max(pairs - 1, 1),
+    unless ``freqs`` gives w; the per-step rotation is the Cayley form
+    ((1 - w^2) / (1 + w^2), 2w / (1 + w^2)); row m is the m-fold product,
+    renormalised to unit length after every step.
+    """
+    if dim <= 0 or dim % 2 != 0:
+        raise ValueError("dim must be a positive even integer")
+    if max_seq_len <= 0:
+        raise ValueError("max_seq_len must be a positive integer")
+    pairs = dim // 2
+    if freqs is not None:
+        w = np.asarray(freqs, dtype=np.float64)
+    else:
+        kk = np.arange(pairs, dtype=np.float64)
+        alpha = (np.sqrt(base) - 1.0) / max(float(pairs - 1), 1.0)
+        lin = 1.0 + alpha * kk
+        w = 1.0 / (lin * lin)
+    c_step = (1.0 - w * w) / (1.0 + w * w)
+    s_step = (2.0 * w) / (1.0 + w * w)
+    c = np.empty((max_seq_len, pairs))
+    s = np.empty((max_seq_len, pairs))
+    cur_c, cur_s = np.ones(pairs), np.zeros(pairs)
+    for m in range(max_seq_len):
+        c[m], s[m] = cur_c, cur_s
+        nc = c_step * cur_c - s_step * cur_s
+        ns = s_step * cur_c + c_step * cur_s
+        norm = 1.0 / np.sqrt(nc * nc + ns * ns)
+        cur_c, cur_s = nc * norm, ns * norm
+    return c, s
+
+
+def ago_seq_axis(shape):
+    """The reference's default sequence axis (reference_ago.py:65-66): 0 for 2-D,
+    1 for 3-D, and for 4-D axis 1 if shape[1] > shape[2] else 2."""
+    ndim = len(shape)
+    return 0 if ndim == 2 else 1 if ndim == 3 else (1 if shape[1] > shape[2] else 2)
+
+
+def ago_rotate(q, k, c=None, s=None, seq_axis=None):
+    """(q_rot, k_rot) in float64 (reference_ago.py:56-94); tables from
+    ``cayley_tables(dim, seq_len)`` when not given."""
+    q = np.asarray(q, dtype=np.float64)
+    k = np.asarray(k, dtype=np.float64)
+    pairs = q.shape[-1] // 2
+    if seq_axis is None:
+        seq_axis = ago_seq_axis(q.shape)
+    n = q.shape[seq_axis]
+    if c is None:
+        c, s = cayley_tables(q.shape[-1], n)
+    shape = [1] * (q.ndim - 1) + [pairs]
+    shape[seq_axis] = n
+    cb = np.asarray(c, dtype=np.float64)[:n].reshape(shape)
+    sb = np.asarray(s, dtype=np.float64)[:n].reshape(shape)
+
+    def rot(x):
+        xp = x.reshape(x.shape[:-1] + (pairs, 2))
+        return np.stack([cb * xp[..., 0] - sb * xp[..., 1], sb * xp[..., 0] + cb * xp[..., 1]],
+                        axis=-1).reshape(x.shape)
+
+    return rot(q), rot(k)
 
 
 def zigzag_chunks(rank, world):

@@ -28,6 +28,16 @@ def golden_meta():
     return json.loads((GOLDEN / "golden_meta.json").read_text())
 
 
+@pytest.fixture(scope="session")
+def golden_ago():
+    """AGO fixtures from the reference's tests/reference_ago.py, with their metadata."""
+    import json
+    with np.load(GOLDEN / "golden_ago.npz") as z:
+        data = {k: z[k] for k in z.files}
+    data["_meta"] = json.loads((GOLDEN / "golden_ago_meta.json").read_text())
+    return data
+
+
 def _cuda_ok():
     try:
         import torch

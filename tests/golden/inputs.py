@@ -62,3 +62,20 @@ def decode_small():
     k = rng.normal(size=(2, 4, 300, 64)).astype(np.float32)
     v = rng.normal(size=(2, 4, 300, 64)).astype(np.float32)
     return q, k, v
+
+
+def ago_small():
+    """AGO rotation input in the reference test's (batch, seq, heads, dim)
+    layout (tests/test_ago.py:29-38), seed 42, shorter sequence."""
+    rng = np.random.default_rng(42)
+    q = rng.standard_normal((2, 16, 4, 32))
+    k = rng.standard_normal((2, 16, 4, 32))
+    return q, k
+
+
+def ago_bhtd():
+    """AGO rotation input in the attention layout (batch, heads, seq, dim)."""
+    rng = np.random.default_rng(43)
+    q = rng.standard_normal((1, 2, 32, 16))
+    k = rng.standard_normal((1, 2, 32, 16))
+    return q, k

@@ -4,9 +4,10 @@ Run in a container that has the reference checkout (it is not needed afterwards)
 
     python tests/golden/make_golden.py /path/to/algebraic-intelligence
 
-The script imports ``tests/reference_attention.py`` of the reference (pure NumPy,
-float64) *read-only* from the given checkout and evaluates it on the seeded
-inputs of ``inputs.py``. The reference's own tests seed with JAX PRNG keys,
+The script imports ``tests/reference_attention.py`` and ``tests/reference_ago.py``
+of the reference (pure NumPy, float64) *read-only* from the given checkout and
+evaluates them on the seeded inputs of ``inputs.py``; the attention fixtures go
+to ``golden.npz``, the AGO rotation fixtures to ``golden_ago.npz``. The reference's own tests seed with JAX PRNG keys,
 which cannot be regenerated without JAX, so NumPy ``default_rng`` seeds are used
 instead. Inputs are not stored; their SHA-256 is, and the tests regenerate them
 and check the digest. Small outputs are stored in float64; the two larger ones
@@ -28,12 +29,48 @@ sys.path.insert(0, str(HERE))
 import inputs  # noqa: E402
 
 
-def _load_reference_oracle(root: Path):
-    path = root / "tests" / "reference_attention.py"
-    spec = importlib.util.spec_from_file_location("_ref_attention_oracle", path)
+def _load_reference_oracle(root: Path, name: str = "reference_attention.py"):
+    path = root / "tests" / name
+    spec = importlib.util.spec_from_file_location("_ref_oracle_" + name.split(".")[0], path)
     mod = importlib.util.module_from_spec(spec)
     spec.loader.exec_module(mod)
     return mod, path
+
+
+AGO_TABLE_ROWS = [0, 1, 2, 3, 127, 128, 1000, 4095]
+
+
+def make_ago(root: Path) -> None:
+    """AGO tables and rotations from tests/reference_ago.py."""
+    ref, path = _load_reference_oracle(root, "reference_ago.py")
+    out, digests = {}, {}
+    c, s = ref.build_cayley_rotary_matrix_fp64(32, 64)
+    out["table_d32_l64_c"], out["table_d32_l64_s"] = c, s
+    c, s = ref.build_cayley_rotary_matrix_fp64(128, 4096)
+    out["table_d128_l4096_rows_c"], out["table_d128_l4096_rows_s"] = c[AGO_TABLE_ROWS], s[AGO_TABLE_ROWS]
+    freqs = np.array([0.9, 0.5, 0.1, 0.01])
+    c, s = ref.build_cayley_rotary_matrix_fp64(8, 16, freqs=freqs)
+    out["table_d8_l16_freqs_c"], out["table_d8_l16_freqs_s"] = c, s
+    c, s = ref.build_cayley_rotary_matrix_fp64(16, 8, base=500.0)
+    out["table_d16_l8_base500_c"], out["table_d16_l8_base500_s"] = c, s
+    q, k = inputs.ago_small()
+    digests["ago_small"] = inputs.digest(q, k)
+    out["ago_small_q"], out["ago_small_k"] = ref.apply_ago_rotations_fp64(q, k)
+    q, k = inputs.ago_bhtd()
+    digests["ago_bhtd"] = inputs.digest(q, k)
+    out["ago_bhtd_q"], out["ago_bhtd_k"] = ref.apply_ago_rotations_fp64(q, k, seq_axis=2)
+    np.savez_compressed(HERE / "golden_ago.npz", **out)
+    meta = {
+        "generator": "tests/golden/make_golden.py",
+        "reference_file": "tests/reference_ago.py",
+        "reference_file_sha256": hashlib.sha256(path.read_bytes()).hexdigest(),
+        "numpy": np.__version__,
+        "input_sha256": digests,
+        "table_d128_l4096_rows": AGO_TABLE_ROWS,
+        "keys": sorted(out),
+    }
+    (HERE / "golden_ago_meta.json").write_text(json.dumps(meta, indent=1) + "\n")
+    print(f"wrote {len(out)} arrays to {HERE / 'golden_ago.npz'}")
 
 
 def main(root: str) -> None:
@@ -89,4 +126,6 @@ def main(root: str) -> None:
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    root = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
+    main(root)
+    make_ago(Path(root))

@@ -123,3 +123,17 @@ def test_backward_argument_checks():
     assert lib.afa_bwd(*ptrs, 1, 1, 64, 64, _lib.AFA_BF16, 0, 65, 1, 1 << 20, None) == _lib.AFA_ERR_INVALID
     assert lib.afa_bwd(*ptrs, 1, 1, 64, 64, _lib.AFA_BF16, 0, 0, 1, 16, None) == _lib.AFA_ERR_INVALID
     assert b"workspace" in lib.afa_last_error()
+
+
+def test_ago_argument_checks():
+    lib = _lib.load()
+    assert lib.afa_ago_table(1, 1, 7, 16, None, 10000.0, _lib.AFA_F32, None) == _lib.AFA_ERR_INVALID
+    assert b"even" in lib.afa_last_error()
+    assert lib.afa_ago_table(1, 1, 8, 0, None, 10000.0, _lib.AFA_F32, None) == _lib.AFA_ERR_INVALID
+    assert lib.afa_ago_table(1, 1, 1026, 4, None, 10000.0, _lib.AFA_F32, None) == _lib.AFA_ERR_INVALID
+    assert lib.afa_ago_table(None, 1, 8, 4, None, 10000.0, _lib.AFA_F32, None) == _lib.AFA_ERR_INVALID
+    assert lib.afa_ago_table(1, 1, 8, 4, None, -1.0, _lib.AFA_F32, None) == _lib.AFA_ERR_INVALID
+    assert lib.afa_ago_table(1, 1, 8, 4, None, 10000.0, _lib.AFA_F16, None) == _lib.AFA_ERR_DTYPE
+    assert lib.afa_ago_rotate(None, 1, 1, 1, 1, 1, _lib.AFA_F32, 4, 8, 4, 1, _lib.AFA_F32, None) == _lib.AFA_ERR_INVALID
+    assert lib.afa_ago_rotate(1, 1, 1, 1, 1, 1, _lib.AFA_F32, 4, 7, 4, 1, _lib.AFA_F32, None) == _lib.AFA_ERR_INVALID
+    assert lib.afa_ago_rotate(1, 1, 1, 1, 1, 1, _lib.AFA_F32, 0, 8, 4, 1, _lib.AFA_F32, None) == _lib.AFA_OK

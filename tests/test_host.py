@@ -96,6 +96,25 @@ def test_backward_argument_errors():
         afa.tiled_afa_backward(xi, xi, xi, xi, d, xi)
 
 
+def test_ago_argument_errors():
+    """src/attention.py:175-178, :222-226."""
+    with pytest.raises(ValueError, match="positive even"):
+        afa.build_cayley_rotary_matrix(7, 16)
+    with pytest.raises(ValueError, match="max_seq_len"):
+        afa.build_cayley_rotary_matrix(8, 0)
+    with pytest.raises(ValueError, match="freqs must have shape"):
+        afa.build_cayley_rotary_matrix(8, 4, freqs=[0.5, 0.5])
+    with pytest.raises(ValueError, match="shapes must match"):
+        afa.apply_ago_rotations(np.ones((4, 8)), np.ones((4, 6)))
+    with pytest.raises(ValueError, match="must be even"):
+        afa.apply_ago_rotations(np.ones((4, 7)), np.ones((4, 7)))
+    with pytest.raises(TypeError):
+        afa.apply_ago_rotations(np.ones((4, 8), dtype=np.int32), np.ones((4, 8), dtype=np.int32))
+    with pytest.raises(TypeError, match="Unsupported rotary"):
+        from algebraic_intelligence_b200.ago import _extract_cs
+        _extract_cs(3.0)
+
+
 # ---------------------------------------------------------------------------
 # Ring plan
 # ---------------------------------------------------------------------------

@@ -149,3 +149,47 @@ def test_backward_oracle_blocking_is_exact():
     b = orc.afa_backward(q, k, v, g, causal=True, block=512)
     for x, y in zip(a, b):
         assert np.max(np.abs(x - y)) <= 1e-12 * np.max(np.abs(y))
+
+
+# ---------------------------------------------------------------------------
+# AGO rotary tables and rotation (tests/reference_ago.py)
+# ---------------------------------------------------------------------------
+def test_ago_inputs_regenerate(golden_ago):
+    want = golden_ago["_meta"]["input_sha256"]
+    assert inputs.digest(*inputs.ago_small()) == want["ago_small"]
+    assert inputs.digest(*inputs.ago_bhtd()) == want["ago_bhtd"]
+
+
+def test_cayley_tables_match_reference(golden_ago):
+    for key, args in (("table_d32_l64", dict(dim=32, max_seq_len=64)),
+                      ("table_d8_l16_freqs", dict(dim=8, max_seq_len=16, freqs=[0.9, 0.5, 0.1, 0.01])),
+                      ("table_d16_l8_base500", dict(dim=16, max_seq_len=8, base=500.0))):
+        c, s = orc.cayley_tables(**args)
+        assert np.array_equal(c, golden_ago[key + "_c"]) and np.array_equal(s, golden_ago[key + "_s"]), key
+    rows = golden_ago["_meta"]["table_d128_l4096_rows"]
+    c, s = orc.cayley_tables(128, 4096)
+    assert np.array_equal(c[rows], golden_ago["table_d128_l4096_rows_c"])
+    assert np.array_equal(s[rows], golden_ago["table_d128_l4096_rows_s"])
+
+
+def test_cayley_tables_are_unit_rotations():
+    """|R| = 1 at every position (the renormalisation), R_0 = identity."""
+    c, s = orc.cayley_tables(64, 2048)
+    assert np.max(np.abs(c * c + s * s - 1.0)) <= 1e-14
+    assert np.all(c[0] == 1.0) and np.all(s[0] == 0.0)
+
+
+def test_ago_rotation_matches_reference(golden_ago):
+    q, k = inputs.ago_small()
+    qr, kr = orc.ago_rotate(q, k)
+    assert np.array_equal(qr, golden_ago["ago_small_q"]) and np.array_equal(kr, golden_ago["ago_small_k"])
+    q, k = inputs.ago_bhtd()
+    qr, kr = orc.ago_rotate(q, k, seq_axis=2)
+    assert np.array_equal(qr, golden_ago["ago_bhtd_q"]) and np.array_equal(kr, golden_ago["ago_bhtd_k"])
+
+
+def test_ago_seq_axis_defaults():
+    assert orc.ago_seq_axis((64, 8)) == 0
+    assert orc.ago_seq_axis((2, 64, 8)) == 1
+    assert orc.ago_seq_axis((2, 64, 4, 8)) == 1
+    assert orc.ago_seq_axis((2, 4, 64, 8)) == 2
