@@ -14,7 +14,7 @@ this package is the host side.
 from .afa import (afa_decode, algebraic_flash_attention, decode_workspace_bytes, pallas_afa, pallas_afa_forward,
                   tiled_afa_backward, tiled_afa_forward)
 from .ago import CayleyRotary, apply_ago_rotations, build_cayley_rotary_matrix
-from .attention import algebraic_softmax, octic_kernel
+from .attention import algebraic_softmax, algebraic_softmax_vjp, octic_kernel
 from .ring import distributed_ring_afa, ring_plan, shard_sequence, unshard_sequence
 
 __all__ = [
@@ -26,6 +26,7 @@ __all__ = [
     "afa_decode",
     "decode_workspace_bytes",
     "algebraic_softmax",
+    "algebraic_softmax_vjp",
     "octic_kernel",
     "CayleyRotary",
     "build_cayley_rotary_matrix",

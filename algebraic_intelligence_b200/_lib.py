@@ -43,6 +43,8 @@ SIGNATURES = {
     "afa_decode_noalloc": (_c_int, [_c_void_p] * 5 + [_c_int] * 5 + [_c_float, _c_void_p, _c_int, _c_void_p]),
     "algebraic_softmax_fwd": (_c_int, [_c_void_p, _c_void_p, _c_ll, _c_int, _c_int, _c_double, _c_double,
                                        _c_void_p]),
+    "algebraic_softmax_bwd": (_c_int, [_c_void_p, _c_void_p, _c_void_p, _c_ll, _c_int, _c_int, _c_double, _c_double,
+                                       _c_void_p]),
     "afa_octic": (_c_int, [_c_void_p, _c_void_p, _c_ll, _c_int, _c_void_p]),
     "afa_device_status": (_c_int, [_c_void_p, ctypes.POINTER(ctypes.c_int), _c_int]),
     "afa_selftest_bounded_wait": (_c_int, [_c_ll, _c_void_p]),

@@ -264,6 +264,21 @@ int algebraic_softmax_fwd(const void* x, void* y, long long rows, int cols, int 
   return AFA_OK;
 }
 
+int algebraic_softmax_bwd(const void* x, const void* g, void* dx, long long rows, int cols, int dtype,
+                          double sink_omega, double eps, void* stream) {
+  if (!(std::isfinite(sink_omega) && sink_omega >= 0.0))
+    return fail(AFA_ERR_INVALID, "sink_omega must be finite and nonnegative");
+  if (!(std::isfinite(eps) && eps > 0.0)) return fail(AFA_ERR_INVALID, "eps must be finite and positive");
+  if (dtype != AFA_F32 && dtype != AFA_BF16 && dtype != AFA_F16 && dtype != AFA_F64)
+    return fail(AFA_ERR_DTYPE, "expected a floating point array");
+  if (cols <= 0 || rows < 0) return fail(AFA_ERR_INVALID, "AVN needs a nonempty feature axis");
+  if (rows > 0 && (!x || !g || !dx)) return fail(AFA_ERR_INVALID, "x, g and dx must be non-null device pointers");
+  cudaError_t e = afa::launch_softmax_bwd(x, g, dx, rows, cols, dtype, sink_omega, eps,
+                                          static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "algebraic_softmax backward launch");
+  return AFA_OK;
+}
+
 int afa_octic(const void* x, void* y, long long n, int dtype, void* stream) {
   if (dtype != AFA_F32 && dtype != AFA_BF16 && dtype != AFA_F16 && dtype != AFA_F64)
     return fail(AFA_ERR_DTYPE, "expected a floating point array");

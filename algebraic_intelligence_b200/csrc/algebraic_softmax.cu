@@ -10,6 +10,13 @@
 // elements are held in the registers of one warp; longer rows use a CTA per
 // row and three sweeps that hit L2 after the first.
 //
+// Backward (the custom VJP of attention.py:70-85 with primitives.py:73-79):
+// with y = tau z, r = rsqrt(1 + y^2), p as above and upstream g,
+//     ng = 8 r p (g - sum(p g))                (attention.py:77-79)
+//     dx = tau (ng - y sum(ng y) / K)          (AVN backward)
+// in the accumulation dtype, returned in g's dtype. The forward quantities
+// are recomputed from x, so the backward reads x and g and writes dx.
+//
 // octic_kernel (attention.py:47-50): y = rho(x)^8 elementwise in the
 // accumulation dtype, returned in the input dtype.
 #include "afa_common.cuh"
@@ -106,6 +113,133 @@ __global__ void __launch_bounds__(256) softmax_block_kernel(const T* __restrict_
     yr[c] = from_acc<T>(octic_ref(static_cast<A>(to_acc(xr[c])) * tau) / den);
 }
 
+// Backward, one warp per row (rows of at most 32 * VPT elements).
+template <typename T, int VPT>
+__global__ void __launch_bounds__(256) softmax_bwd_warp_kernel(const T* __restrict__ x, const T* __restrict__ g,
+                                                               T* __restrict__ dx, long long rows, int cols,
+                                                               double sink_d, double eps_d) {
+  using A = typename AccOf<T>::type;
+  const long long row = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  const T* xr = x + row * cols;
+  const T* gr = g + row * cols;
+  T* dr = dx + row * cols;
+  const A inv_width = static_cast<A>(1.0 / cols);
+  A y[VPT], p[VPT], gv[VPT];
+  A ss = A(0);
+#pragma unroll
+  for (int i = 0; i < VPT; ++i) {
+    const int c = lane + 32 * i;
+    y[i] = c < cols ? static_cast<A>(to_acc(xr[c])) : A(0);
+    gv[i] = c < cols ? static_cast<A>(to_acc(gr[c])) : A(0);
+    ss = fma(y[i], y[i], ss);
+  }
+  const A tau = rsqrt_acc<A>(warp_sum(ss) * inv_width + static_cast<A>(eps_d));
+  A ks = A(0);
+#pragma unroll
+  for (int i = 0; i < VPT; ++i) {
+    const int c = lane + 32 * i;
+    y[i] *= tau;
+    p[i] = c < cols ? octic_ref(y[i]) : A(0);
+    ks += p[i];
+  }
+  const A inv_den = A(1) / (warp_sum(ks) + static_cast<A>(sink_d));
+  A pg = A(0);
+#pragma unroll
+  for (int i = 0; i < VPT; ++i) {
+    p[i] *= inv_den;
+    pg = fma(p[i], gv[i], pg);
+  }
+  pg = warp_sum(pg);
+  A ny = A(0);
+#pragma unroll
+  for (int i = 0; i < VPT; ++i) {
+    const A r = rsqrt_acc<A>(fma(y[i], y[i], A(1)));
+    gv[i] = A(8) * r * p[i] * (gv[i] - pg);  // ng
+    ny = fma(gv[i], y[i], ny);
+  }
+  const A radial = warp_sum(ny) * inv_width;
+#pragma unroll
+  for (int i = 0; i < VPT; ++i) {
+    const int c = lane + 32 * i;
+    if (c < cols) dr[c] = from_acc<T>(tau * (gv[i] - radial * y[i]));
+  }
+}
+
+// Backward, one CTA per row (longer rows): five sweeps over the row, all but
+// the first from L2.
+template <typename T>
+__global__ void __launch_bounds__(256) softmax_bwd_block_kernel(const T* __restrict__ x, const T* __restrict__ g,
+                                                                T* __restrict__ dx, int cols, double sink_d,
+                                                                double eps_d) {
+  using A = typename AccOf<T>::type;
+  __shared__ A red[8];
+  const long long row = blockIdx.x;
+  const T* xr = x + row * cols;
+  const T* gr = g + row * cols;
+  T* dr = dx + row * cols;
+  const A inv_width = static_cast<A>(1.0 / cols);
+  A ss = A(0);
+  for (int c = threadIdx.x; c < cols; c += blockDim.x) {
+    const A z = static_cast<A>(to_acc(xr[c]));
+    ss = fma(z, z, ss);
+  }
+  const A tau = rsqrt_acc<A>(block_sum(ss, red) * inv_width + static_cast<A>(eps_d));
+  A ks = A(0);
+  for (int c = threadIdx.x; c < cols; c += blockDim.x) ks += octic_ref(static_cast<A>(to_acc(xr[c])) * tau);
+  const A inv_den = A(1) / (block_sum(ks, red) + static_cast<A>(sink_d));
+  A pg = A(0);
+  for (int c = threadIdx.x; c < cols; c += blockDim.x)
+    pg = fma(octic_ref(static_cast<A>(to_acc(xr[c])) * tau) * inv_den, static_cast<A>(to_acc(gr[c])), pg);
+  pg = block_sum(pg, red);
+  auto ng_of = [&](int c, A& yv) {
+    yv = static_cast<A>(to_acc(xr[c])) * tau;
+    const A pv = octic_ref(yv) * inv_den;
+    return A(8) * rsqrt_acc<A>(fma(yv, yv, A(1))) * pv * (static_cast<A>(to_acc(gr[c])) - pg);
+  };
+  A ny = A(0);
+  for (int c = threadIdx.x; c < cols; c += blockDim.x) {
+    A yv;
+    const A ng = ng_of(c, yv);
+    ny = fma(ng, yv, ny);
+  }
+  const A radial = block_sum(ny, red) * inv_width;
+  for (int c = threadIdx.x; c < cols; c += blockDim.x) {
+    A yv;
+    const A ng = ng_of(c, yv);
+    dr[c] = from_acc<T>(tau * (ng - radial * yv));
+  }
+}
+
+template <typename T>
+cudaError_t softmax_bwd_t(const void* x, const void* g, void* dx, long long rows, int cols, double sink, double eps,
+                          cudaStream_t stream) {
+  using A = typename AccOf<T>::type;
+  const T* xp = static_cast<const T*>(x);
+  const T* gp = static_cast<const T*>(g);
+  T* dp = static_cast<T*>(dx);
+  // Three row arrays stay in registers: up to 1024 float32 or 512 float64 columns.
+  const int warp_limit = sizeof(A) == 8 ? 512 : 1024;
+  if (cols <= warp_limit) {
+    const long long blocks = (rows * 32 + 255) / 256;
+    if (blocks > 2147483647LL) return cudaErrorInvalidValue;
+    const int vpt = (cols + 31) / 32;
+    const dim3 b(static_cast<unsigned>(blocks));
+    if (vpt <= 1) softmax_bwd_warp_kernel<T, 1><<<b, 256, 0, stream>>>(xp, gp, dp, rows, cols, sink, eps);
+    else if (vpt <= 2) softmax_bwd_warp_kernel<T, 2><<<b, 256, 0, stream>>>(xp, gp, dp, rows, cols, sink, eps);
+    else if (vpt <= 4) softmax_bwd_warp_kernel<T, 4><<<b, 256, 0, stream>>>(xp, gp, dp, rows, cols, sink, eps);
+    else if (vpt <= 8) softmax_bwd_warp_kernel<T, 8><<<b, 256, 0, stream>>>(xp, gp, dp, rows, cols, sink, eps);
+    else if (vpt <= 16) softmax_bwd_warp_kernel<T, 16><<<b, 256, 0, stream>>>(xp, gp, dp, rows, cols, sink, eps);
+    else if constexpr (sizeof(A) == 4)
+      softmax_bwd_warp_kernel<T, 32><<<b, 256, 0, stream>>>(xp, gp, dp, rows, cols, sink, eps);
+  } else {
+    if (rows > 2147483647LL) return cudaErrorInvalidValue;
+    softmax_bwd_block_kernel<T><<<static_cast<unsigned>(rows), 256, 0, stream>>>(xp, gp, dp, cols, sink, eps);
+  }
+  return cudaGetLastError();
+}
+
 template <typename T>
 __global__ void octic_kernel(const T* __restrict__ x, T* __restrict__ y, long long n) {
   using A = typename AccOf<T>::type;
@@ -156,6 +290,18 @@ cudaError_t launch_softmax(const void* x, void* y, long long rows, int cols, int
     case kBF16: return softmax_t<__nv_bfloat16>(x, y, rows, cols, sink, eps, stream);
     case kF16: return softmax_t<__half>(x, y, rows, cols, sink, eps, stream);
     case kF64: return softmax_t<double>(x, y, rows, cols, sink, eps, stream);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+cudaError_t launch_softmax_bwd(const void* x, const void* g, void* dx, long long rows, int cols, int dtype, double sink,
+                               double eps, cudaStream_t stream) {
+  if (rows == 0) return cudaSuccess;
+  switch (dtype) {
+    case kF32: return softmax_bwd_t<float>(x, g, dx, rows, cols, sink, eps, stream);
+    case kBF16: return softmax_bwd_t<__nv_bfloat16>(x, g, dx, rows, cols, sink, eps, stream);
+    case kF16: return softmax_bwd_t<__half>(x, g, dx, rows, cols, sink, eps, stream);
+    case kF64: return softmax_bwd_t<double>(x, g, dx, rows, cols, sink, eps, stream);
     default: return cudaErrorInvalidValue;
   }
 }

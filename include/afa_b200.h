@@ -22,6 +22,7 @@
  *   afa_decode            <- no reference counterpart: exact AFA for one query
  *                            token over a KV cache (pallas_afa_forward with Lq=1)
  *   algebraic_softmax_fwd <- algebraic_softmax   (src/attention.py:88-91, :59-67)
+ *   algebraic_softmax_bwd <- its custom VJP      (src/attention.py:70-85)
  *   afa_octic             <- octic_kernel        (src/attention.py:47-50) and
  *                            _vmu_octic_kernel   (pallas_afa.py:32-49)
  *
@@ -239,6 +240,16 @@ AFA_API int algebraic_softmax_fwd(const void* x, void* y, long long rows, int co
 
 /* octic_kernel (src/attention.py:47-50): y = rho(x)^8 elementwise, n elements. */
 AFA_API int afa_octic(const void* x, void* y, long long n, int dtype, void* stream);
+
+/*
+ * algebraic_softmax backward: the custom VJP of algebraic_softmax
+ * (src/attention.py:70-85 with the AVN VJP, src/primitives.py:73-79). x: the
+ * forward's input scores, g: the upstream gradient, dx: the input gradient,
+ * all (rows, cols) in `dtype`; the same sink_omega / eps as the forward. The
+ * forward quantities are recomputed from x.
+ */
+AFA_API int algebraic_softmax_bwd(const void* x, const void* g, void* dx, long long rows, int cols, int dtype,
+                                  double sink_omega, double eps, void* stream);
 
 /*
  * Synchronises `stream`, then reads the calling device's status word (0 = no

@@ -15,6 +15,10 @@ It restates, in float64 NumPy, the reference's own ground truth
 * ``attention``        -- tests/reference_attention.py:21-24 (AVN over the last
                           axis, then the sink-normalised octic weights); this is
                           the math of ``algebraic_softmax`` (src/attention.py:59-67).
+* ``attention_vjp``    -- tests/reference_attention.py:27-36: the cotangent of
+                          the scores of ``attention`` by the quotient rule,
+                          independent of the production VJP's cached-p form
+                          (src/attention.py:70-85).
 * ``afa``              -- tests/reference_attention.py:44-59 (``reference_afa``),
                           the exact float64 AFA forward, causal = top-left
                           aligned ``tril``.
@@ -63,6 +67,7 @@ __all__ = [
     "octic",
     "normalized",
     "attention",
+    "attention_vjp",
     "afa",
     "afa_blocked",
     "afa_with_denominator",
@@ -107,6 +112,24 @@ def attention(x, sink=0.5, eps=1e-5):
     x = np.asarray(x, dtype=np.float64)
     z = x / np.sqrt(np.mean(x * x, axis=-1, keepdims=True) + eps)
     return normalized(z, sink)
+
+
+def attention_vjp(x, g, sink=0.5, eps=1e-5):
+    """d/dx of sum(attention(x) * g) in float64 (reference_attention.py:27-36).
+
+    With tau = 1/sqrt(mean(x^2) + eps), z = tau x, k = rho(z)^8 and D = sum(k) +
+    sink: dz = 8 k / sqrt(1 + z^2) * (g / D - sum(g k) / D^2), and the AVN
+    chain gives dx = tau dz - x tau^3 mean(x dz).
+    """
+    x = np.asarray(x, dtype=np.float64)
+    g = np.asarray(g, dtype=np.float64)
+    tau = 1.0 / np.sqrt(np.mean(x * x, axis=-1, keepdims=True) + eps)
+    z = tau * x
+    k = octic(z)
+    den = np.sum(k, axis=-1, keepdims=True) + sink
+    dk = 8.0 * k / np.sqrt(1.0 + z * z)
+    dz = dk * (g / den - np.sum(g * k, axis=-1, keepdims=True) / den ** 2)
+    return tau * dz - x * tau ** 3 * np.mean(x * dz, axis=-1, keepdims=True)
 
 
 def afa(q, k, v, sink=0.5, causal=False):

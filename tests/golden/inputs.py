@@ -79,3 +79,15 @@ def ago_bhtd():
     q = rng.standard_normal((1, 2, 32, 16))
     k = rng.standard_normal((1, 2, 32, 16))
     return q, k
+
+
+def softmax_vjp():
+    """Scores and cotangents as tests/test_attention.py:16-20 draws them
+    (default_rng(42), normal (4, 128)), plus one 3000-column pair."""
+    rng = np.random.default_rng(42)
+    x = rng.normal(size=(4, 128))
+    g = rng.normal(size=(4, 128))
+    rng = np.random.default_rng(9)
+    xl = rng.normal(size=(2, 3000)) * 3.0
+    gl = rng.normal(size=(2, 3000))
+    return x, g, xl, gl

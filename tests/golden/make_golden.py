@@ -108,6 +108,12 @@ def main(root: str) -> None:
     out["cfg1_softmax_o"] = np.matmul(ref.attention(s, 0.5, 1e-5), v.astype(np.float64)).astype(np.float32)
     out["cfg1_afa_o"] = ref.reference_afa(q, k, v, sink=0.5, causal=False).astype(np.float32)
 
+    x, g, xl, gl = inputs.softmax_vjp()
+    digests["softmax_vjp"] = inputs.digest(x, g, xl, gl)
+    for sink in (0.0, 0.5, 1.0):
+        out[f"asm_vjp_sink{sink}"] = ref.attention_vjp(x, g, sink)
+    out["asm_vjp_long"] = ref.attention_vjp(xl, gl, 0.5)
+
     q, k, v = inputs.decode_small()
     digests["decode_small"] = inputs.digest(q, k, v)
     out["dec_y"] = ref.reference_afa(q, k, v, sink=0.5, causal=False)

@@ -280,3 +280,61 @@ def test_bounded_wait_reports_instead_of_hanging():
     assert _lib.device_status(dev) == 0
     x = to_dev(inputs.softmax_rows(), torch.float32)
     np.testing.assert_allclose(host64(afa.algebraic_softmax(x)), orc.attention(host64(x)), rtol=2e-5, atol=2e-5)
+
+
+# ---------------------------------------------------------------------------
+# algebraic_softmax backward (the custom VJP, src/attention.py:70-85)
+# ---------------------------------------------------------------------------
+@pytest.mark.parametrize("dtype,tol", [(torch.float64, 2e-13), (torch.float32, 2e-5), (torch.bfloat16, 0.016)])
+@pytest.mark.parametrize("sink", [0.0, 0.5, 1.0])
+def test_softmax_vjp_golden(golden, dtype, tol, sink):
+    """tests/test_attention.py:14-26: the VJP against the reference oracle's
+    attention_vjp, with the same rtol = atol per dtype."""
+    x, g, _, _ = inputs.softmax_vjp()
+    xt = torch.as_tensor(x, device="cuda").to(dtype)
+    gt = torch.as_tensor(g, device="cuda").to(dtype)
+    dx = afa.algebraic_softmax_vjp(xt, gt, sink)
+    assert dx.dtype == dtype
+    # The oracle ran on the float64 draws; for bf16 compare on the rounded inputs.
+    want = golden[f"asm_vjp_sink{sink}"] if dtype != torch.bfloat16 else orc.attention_vjp(
+        xt.double().cpu().numpy(), gt.double().cpu().numpy(), sink)
+    np.testing.assert_allclose(dx.double().cpu().numpy(), want, rtol=tol, atol=tol)
+
+
+@pytest.mark.parametrize("dtype,tol", [(torch.float64, 1e-12), (torch.float32, 2e-5)])
+def test_softmax_vjp_long_rows(golden, dtype, tol):
+    """3000 columns: the CTA-per-row backward kernel."""
+    _, _, xl, gl = inputs.softmax_vjp()
+    dx = afa.algebraic_softmax_vjp(torch.as_tensor(xl, device="cuda").to(dtype),
+                                   torch.as_tensor(gl, device="cuda").to(dtype), 0.5)
+    want = golden["asm_vjp_long"]
+    assert np.max(np.abs(dx.double().cpu().numpy() - want)) <= tol * np.max(np.abs(want)) * 10
+
+
+@pytest.mark.parametrize("cols", [1, 31, 200, 512, 1000, 1024, 1500])
+@pytest.mark.parametrize("dtype", [torch.float64, torch.float32])
+def test_softmax_autograd_against_oracle(cols, dtype):
+    """torch autograd through algebraic_softmax (jax.vjp in the reference),
+    every warp-row width and the CTA path."""
+    g0 = torch.Generator(device="cuda").manual_seed(cols)
+    x = torch.randn((5, cols), generator=g0, device="cuda", dtype=torch.float64).to(dtype).requires_grad_(True)
+    g = torch.randn((5, cols), generator=g0, device="cuda", dtype=torch.float64).to(dtype)
+    y = afa.algebraic_softmax(x, 0.5)
+    y.backward(g)
+    want = orc.attention_vjp(x.detach().double().cpu().numpy(), g.double().cpu().numpy(), 0.5)
+    tol = 1e-12 if dtype == torch.float64 else 2e-5
+    assert np.max(np.abs(x.grad.double().cpu().numpy() - want)) <= tol * max(1.0, np.max(np.abs(want)))
+
+
+def test_softmax_vjp_float16_and_numpy():
+    rng = np.random.default_rng(3)
+    x, g = rng.normal(size=(4, 64)), rng.normal(size=(4, 64))
+    dx = afa.algebraic_softmax_vjp(x, g, 0.5)
+    assert isinstance(dx, np.ndarray)
+    assert np.max(np.abs(dx - orc.attention_vjp(x, g, 0.5))) <= 1e-12
+    xh = torch.as_tensor(x, device="cuda").half()
+    gh = torch.as_tensor(g, device="cuda").half()
+    dxh = afa.algebraic_softmax_vjp(xh, gh, 0.5)
+    want = orc.attention_vjp(xh.double().cpu().numpy(), gh.double().cpu().numpy(), 0.5)
+    assert dxh.dtype == torch.float16
+    np.testing.assert_allclose(dxh.double().cpu().numpy(), want, rtol=0.016, atol=0.016)

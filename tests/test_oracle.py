@@ -193,3 +193,27 @@ def test_ago_seq_axis_defaults():
     assert orc.ago_seq_axis((2, 64, 8)) == 1
     assert orc.ago_seq_axis((2, 64, 4, 8)) == 1
     assert orc.ago_seq_axis((2, 4, 64, 8)) == 2
+
+
+# ---------------------------------------------------------------------------
+# algebraic_softmax VJP (tests/reference_attention.py:27-36)
+# ---------------------------------------------------------------------------
+def test_softmax_vjp_matches_reference(golden, golden_meta):
+    assert inputs.digest(*inputs.softmax_vjp()) == golden_meta["input_sha256"]["softmax_vjp"]
+    x, g, xl, gl = inputs.softmax_vjp()
+    for sink in (0.0, 0.5, 1.0):
+        assert np.array_equal(orc.attention_vjp(x, g, sink), golden[f"asm_vjp_sink{sink}"])
+    assert np.array_equal(orc.attention_vjp(xl, gl, 0.5), golden["asm_vjp_long"])
+
+
+def test_softmax_vjp_finite_differences():
+    rng = np.random.default_rng(5)
+    x, g = rng.normal(size=(3, 17)), rng.normal(size=(3, 17))
+    grad = orc.attention_vjp(x, g, 0.5)
+    h = 1e-6
+    for idx in [(0, 0), (1, 5), (2, 16)]:
+        xp, xm = x.copy(), x.copy()
+        xp[idx] += h
+        xm[idx] -= h
+        fd = (np.sum(orc.attention(xp, 0.5) * g) - np.sum(orc.attention(xm, 0.5) * g)) / (2 * h)
+        assert abs(fd - grad[idx]) <= 1e-7 * max(1.0, abs(grad[idx]))
