@@ -164,7 +164,8 @@ __device__ __forceinline__ float map_chunk(const uint32_t (&sv)[32], uint32_t (&
 template <int HD>
 __global__ void __launch_bounds__(576, 1)
     afa_tc_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
-                      const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ Launch L) {
+                      const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_o,
+                      const __grid_constant__ Launch L) {
   using C = TcCfg<HD>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -225,6 +226,7 @@ __global__ void __launch_bounds__(576, 1)
     prefetch_tmap(&tm_q);
     prefetch_tmap(&tm_k);
     prefetch_tmap(&tm_v);
+    prefetch_tmap(&tm_o);
   }
   if (warp == C::kMmaWarp) {
     tmem_alloc(tmem_slot, C::TMEM_COLS);
@@ -391,6 +393,16 @@ __global__ void __launch_bounds__(576, 1)
     const bool fin = L.mode == kFinal || L.mode == kAccumFinal;
     const bool add_prev = L.mode == kAccumRaw || L.mode == kAccumFinal;
     constexpr int OC = HD / 4;  // O columns per warpgroup: 32 (D=128) or 16 (D=64)
+    // A bf16 output tile leaves through a TMA store from shared memory (the
+    // K/V ring is idle now) when its 128 rows all belong to this problem or
+    // run past the end of the tensor, where TMA writes nothing; a direct store
+    // from each thread would touch 32 rows per warp instruction. Other tiles
+    // (a problem ending mid-tile next to another problem's rows) store directly.
+    bool tma_tile[2];
+#pragma unroll
+    for (int tile = 0; tile < 2; ++tile)
+      tma_tile[tile] = fin && r0 + 128 * tile < P.q.len &&
+                       (r0 + 128 * (tile + 1) <= P.q.len || P.q.row0 + P.q.len == L.lq);
 #pragma unroll
     for (int tile = 0; tile < 2; ++tile) {
       const float drow_tile = red[(tile * 4 + 0) * 128 + row] + red[(tile * 4 + 1) * 128 + row] +
@@ -418,46 +430,72 @@ __global__ void __launch_bounds__(576, 1)
 #pragma unroll
         for (int e = 0; e < 32; ++e) ov[e] = 0u;
       }
-      if (row_ok) {
-        float x[OC];
+      float x[OC];
 #pragma unroll
-        for (int e = 0; e < OC; ++e) x[e] = __uint_as_float(ov[e]);
-        if (add_prev) {
-          const float4* src = reinterpret_cast<const float4*>(acc_row);
+      for (int e = 0; e < OC; ++e) x[e] = __uint_as_float(ov[e]);
+      if (row_ok && add_prev) {
+        const float4* src = reinterpret_cast<const float4*>(acc_row);
 #pragma unroll
-          for (int w = 0; w < OC / 4; ++w) {
-            const float4 y = src[w];
-            x[4 * w + 0] += y.x;
-            x[4 * w + 1] += y.y;
-            x[4 * w + 2] += y.z;
-            x[4 * w + 3] += y.w;
-          }
+        for (int w = 0; w < OC / 4; ++w) {
+          const float4 y = src[w];
+          x[4 * w + 0] += y.x;
+          x[4 * w + 1] += y.y;
+          x[4 * w + 2] += y.z;
+          x[4 * w + 3] += y.w;
         }
-        if (fin) {
-          uint4* dst = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(L.out) + grow * HD + OC * g);
+      }
+      if (fin) {
+        uint4 pk[OC / 8];
+#pragma unroll
+        for (int w = 0; w < OC / 8; ++w) {
+          pk[w].x = pack_bf16x2(x[8 * w + 0] * inv, x[8 * w + 1] * inv);
+          pk[w].y = pack_bf16x2(x[8 * w + 2] * inv, x[8 * w + 3] * inv);
+          pk[w].z = pack_bf16x2(x[8 * w + 4] * inv, x[8 * w + 5] * inv);
+          pk[w].w = pack_bf16x2(x[8 * w + 6] * inv, x[8 * w + 7] * inv);
+        }
+        if (tma_tile[tile]) {
+          // 128-byte-swizzled staging: 64-column blocks of 128 rows x 128 B,
+          // 16-byte chunk j of row r at (j ^ (r % 8)) * 16.
+          uint8_t* stage = smem + C::KV_OFF + tile * C::TILE_BYTES;
 #pragma unroll
           for (int w = 0; w < OC / 8; ++w) {
-            uint4 pkt;
-            pkt.x = pack_bf16x2(x[8 * w + 0] * inv, x[8 * w + 1] * inv);
-            pkt.y = pack_bf16x2(x[8 * w + 2] * inv, x[8 * w + 3] * inv);
-            pkt.z = pack_bf16x2(x[8 * w + 4] * inv, x[8 * w + 5] * inv);
-            pkt.w = pack_bf16x2(x[8 * w + 6] * inv, x[8 * w + 7] * inv);
-            dst[w] = pkt;
+            const int col0 = OC * g + 8 * w;
+            const int j = (col0 & 63) >> 3;
+            st_shared_v4(smem_u32(stage + (col0 >> 6) * C::SUB_BYTES + row * 128 + ((j ^ (row & 7)) << 4)), pk[w]);
           }
-        } else {
-          float4* dst = reinterpret_cast<float4*>(acc_row);
+        } else if (row_ok) {
+          uint4* dst = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(L.out) + grow * HD + OC * g);
 #pragma unroll
-          for (int w = 0; w < OC / 4; ++w) dst[w] = make_float4(x[4 * w + 0], x[4 * w + 1], x[4 * w + 2], x[4 * w + 3]);
+          for (int w = 0; w < OC / 8; ++w) dst[w] = pk[w];
         }
-        // d_acc / d_total: one writer per row (warpgroup 0); the others only
-        // read d_acc above, in kAccumFinal, where nothing writes it.
-        if (g == 0) {
-          if (fin) {
-            if (L.dtot) static_cast<float*>(L.dtot)[grow] = denom;
-          } else {
-            static_cast<float*>(L.d_acc)[grow] = drow;
-          }
+      } else if (row_ok) {
+        float4* dst = reinterpret_cast<float4*>(acc_row);
+#pragma unroll
+        for (int w = 0; w < OC / 4; ++w) dst[w] = make_float4(x[4 * w + 0], x[4 * w + 1], x[4 * w + 2], x[4 * w + 3]);
+      }
+      // d_acc / d_total: one writer per row (warpgroup 0); the others only
+      // read d_acc above, in kAccumFinal, where nothing writes it.
+      if (row_ok && g == 0) {
+        if (fin) {
+          if (L.dtot) static_cast<float*>(L.dtot)[grow] = denom;
+        } else {
+          static_cast<float*>(L.d_acc)[grow] = drow;
         }
+      }
+    }
+    if (tma_tile[0] || tma_tile[1]) {  // uniform across the octic warps
+      fence_proxy_async_shared();
+      asm volatile("bar.sync 1, %0;" ::"r"(C::kOcticWarps * 32) : "memory");
+      if (threadIdx.x == 0) {
+#pragma unroll
+        for (int tile = 0; tile < 2; ++tile) {
+          if (!tma_tile[tile]) continue;
+          for (int h = 0; h < C::KSUB; ++h)
+            tma_store_3d(&tm_o, smem + C::KV_OFF + tile * C::TILE_BYTES + h * C::SUB_BYTES, 64 * h,
+                         P.q.row0 + r0 + 128 * tile, bh);
+        }
+        bulk_commit();
+        bulk_wait_read();  // the staging area is released when the CTA exits
       }
     }
   }
@@ -889,10 +927,10 @@ cudaError_t launch_hd(const Launch& L, cudaStream_t stream, const char** detail)
     }
     attr_set[dev] = true;
   }
-  CUtensorMap tq, tk, tv;
+  CUtensorMap tq, tk, tv, to;
   const int bh = L.B * L.H;
   if (!make_tmap(&tq, L.q, HD, L.lq, bh) || !make_tmap(&tk, L.k, HD, L.lk, bh) ||
-      !make_tmap(&tv, L.v, HD, L.lk, bh)) {
+      !make_tmap(&tv, L.v, HD, L.lk, bh) || (L.out && !make_tmap(&to, L.out, HD, L.lq, bh))) {
     *detail = "cuTensorMapEncodeTiled failed (pointer must be 16-byte aligned)";
     return cudaErrorInvalidValue;
   }
@@ -935,8 +973,9 @@ cudaError_t launch_hd(const Launch& L, cudaStream_t stream, const char** detail)
     }
     return cudaGetLastError();
   }
+  if (!L.out) to = tq;  // raw modes store no bf16 output
   dim3 grid(bh, total);
-  afa_tc_fwd_kernel<HD><<<grid, C::kThreads, C::SMEM_BYTES, stream>>>(tq, tk, tv, LL);
+  afa_tc_fwd_kernel<HD><<<grid, C::kThreads, C::SMEM_BYTES, stream>>>(tq, tk, tv, to, LL);
   return cudaGetLastError();
 }
 
