@@ -209,12 +209,37 @@ __global__ void __launch_bounds__(576, 1)
   const int n1 = cnt1[0] + cnt1[1];
   const int n0 = (P.nk == 1 || cnt0[0] == cnt1[0]) ? cnt0[0] + cnt0[1] : n1;
 
-  if (threadIdx.x == 0) {
+  // The TMA thread sets up the barriers its loads complete and issues Q and
+  // the first ring of K/V tiles (the slots start empty: no wait) before the
+  // CTA-wide barrier, so their latency overlaps barrier and TMEM set-up.
+  // Every load that needs a wait comes after it.
+  const int early = n1 > 0 ? (2 * n1 < C::NSLOT ? 2 * n1 : C::NSLOT) : 0;
+  if (warp == C::kTmaWarp && lane == 0) {
     mbar_init(q_full, 1);
     for (int s = 0; s < C::NSLOT; ++s) {
       mbar_init(kv_full + s, 1);
       mbar_init(kv_empty + s, 1);
     }
+    fence_barrier_init();
+    prefetch_tmap(&tm_q);
+    prefetch_tmap(&tm_k);
+    prefetch_tmap(&tm_v);
+    if (n1 > 0) {
+      mbar_arrive_expect_tx(q_full, 2 * C::TILE_BYTES);
+      for (int i = 0; i < 2; ++i)
+        for (int h = 0; h < C::KSUB; ++h)
+          tma_load_3d(smem + C::Q_OFF + (i * C::KSUB + h) * C::SUB_BYTES, &tm_q, q_full, 64 * h,
+                      P.q.row0 + r0 + 128 * i, bh);
+      for (int u = 0; u < early; ++u) {
+        const KvTile kt = kv_tile(P, cnt1[0], u >> 1);
+        mbar_arrive_expect_tx(kv_full + u, C::TILE_BYTES);
+        for (int h = 0; h < C::KSUB; ++h)
+          tma_load_3d(smem + C::KV_OFF + (u * C::KSUB + h) * C::SUB_BYTES, (u & 1) ? &tm_v : &tm_k, kv_full + u,
+                      64 * h, kt.row, bh);
+      }
+    }
+  }
+  if (threadIdx.x == 0) {
     for (int i = 0; i < 2; ++i) {
       mbar_init(s_full + i, 1);
       mbar_init(p_full + i, 16);  // one elected arrive per octic warp
@@ -223,9 +248,6 @@ __global__ void __launch_bounds__(576, 1)
     mbar_init(drain, 1);
     fence_barrier_init();
     fence_proxy_async_smem();
-    prefetch_tmap(&tm_q);
-    prefetch_tmap(&tm_k);
-    prefetch_tmap(&tm_v);
     prefetch_tmap(&tm_o);
   }
   if (warp == C::kMmaWarp) {
@@ -240,17 +262,13 @@ __global__ void __launch_bounds__(576, 1)
   if (warp == C::kTmaWarp) {
     // ------------------------------------------------------------------ TMA
     if (lane == 0 && n1 > 0) {
-      mbar_arrive_expect_tx(q_full, 2 * C::TILE_BYTES);
-      for (int i = 0; i < 2; ++i)
-        for (int h = 0; h < C::KSUB; ++h)
-          tma_load_3d(smem + C::Q_OFF + (i * C::KSUB + h) * C::SUB_BYTES, &tm_q, q_full, 64 * h,
-                      P.q.row0 + r0 + 128 * i, bh);
-      int issued = 0;
-      for (int t = 0; t < n1; ++t) {
+      int issued = early;
+      for (int t = early >> 1; t < n1; ++t) {
         const KvTile kt = kv_tile(P, cnt1[0], t);
         bool ok = true;
         for (int kv = 0; kv < 2; ++kv) {
           const int u = 2 * t + kv;
+          if (u < early) continue;  // issued before the CTA barrier
           const int slot = u % C::NSLOT;
           if (!mbar_wait(kv_empty + slot, ((u / C::NSLOT) & 1) ^ 1, L.status, kDevTimeoutProducer)) {
             ok = false;
