@@ -299,9 +299,16 @@ _EXCHANGES = {}
 
 def get_exchange(shape, dtype: torch.dtype, device: torch.device, group=None) -> CudaIpcExchange:
     """The cached exchange of ``group`` for K/V shards of ``shape`` (B, H, S, D).
-    The first call for a key is collective over the group (it swaps IPC handles)."""
+    The first call for a key is collective over the group (it swaps IPC handles).
+
+    The key holds the process-group object itself (the default group's current
+    object when ``group`` is None), so a group that is destroyed and created
+    again never finds the old group's mappings.
+    """
+    import torch.distributed as dist
     device = torch.device(device)
-    key = (id(group), tuple(shape), dtype, device.index)
+    pg = group if group is not None else dist.group.WORLD
+    key = (pg, tuple(shape), dtype, device.index)
     ex = _EXCHANGES.get(key)
     if ex is None:
         ex = _EXCHANGES[key] = CudaIpcExchange(shape, dtype, device, group)
@@ -370,6 +377,8 @@ def distributed_ring_afa(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, sink
         raise ValueError("sink_omega must be finite and nonnegative")
     if not (q.is_cuda and k.is_cuda and v.is_cuda):
         raise ValueError("ring AFA runs on CUDA tensors (one GPU per rank)")
+    if not (q.dtype == k.dtype == v.dtype):
+        raise TypeError(f"q, k and v must share a dtype, got {q.dtype}, {k.dtype} and {v.dtype}")
     group = axis_name
     if dist.is_available() and dist.is_initialized():
         world = dist.get_world_size(group)
