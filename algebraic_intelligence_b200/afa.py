@@ -17,7 +17,9 @@ Drop-in for the forward entry points of src/kernels/pallas_afa.py
                                    (batch, head) over a KV cache
 
 Arrays are torch CUDA tensors shaped (batch, heads, sequence, dim); NumPy arrays
-and CPU tensors are accepted and staged through the GPU. ``block_q`` /
+and CPU tensors are accepted too. Host inputs of the forward are streamed
+through the GPU in chunks of (batch x heads), the copies of one chunk
+overlapping the kernels of its neighbours (``_launch_fwd_host``). ``block_q`` /
 ``block_k`` and ``interpret`` are validated like the reference but do not
 change the computation: the B200 kernels tile at 128 x 128 on the tensor cores
 and the result of the additive accumulation does not depend on the tiling
@@ -52,7 +54,77 @@ def _sink_ok(sink_omega) -> bool:
         return False
 
 
+def _is_host(a) -> bool:
+    return isinstance(a, np.ndarray) or (isinstance(a, torch.Tensor) and not a.is_cuda)
+
+
+def _launch_fwd_host(q, k, v, sink_omega, causal, valid_seq_len, return_denominator):
+    """Forward of host arrays, pipelined over chunks of (batch x heads).
+
+    Chunk c's H2D copies run on an upload stream while chunk c-1 computes, and
+    chunk c's output copies back on a download stream while chunk c+1
+    computes, so PCIe traffic and the kernels overlap (the copy engines carry
+    the transfers; from pinned memory they are fully asynchronous). Chunks hold
+    about two SM-waves of query pairs. Returns host arrays of the input kind
+    once the results are in host memory.
+    """
+    as_numpy = isinstance(q, np.ndarray)
+    qh, kh, vh = (torch.from_numpy(np.ascontiguousarray(a)) if isinstance(a, np.ndarray) else a.contiguous()
+                  for a in (q, k, v))
+    if not (qh.dtype == kh.dtype == vh.dtype):
+        raise TypeError(f"q, k and v must share a dtype, got {qh.dtype}, {kh.dtype} and {vh.dtype}")
+    if not torch.cuda.is_available():
+        raise RuntimeError("a CUDA device is required: this library has no CPU execution path")
+    code = _lib.dtype_code(qh.dtype)
+    b, h, l, d = qh.shape
+    bh = b * h
+    dev = torch.device("cuda", torch.cuda.current_device())
+    props = torch.cuda.get_device_properties(dev)
+    per = max(1, min(bh, -(-2 * props.multi_processor_count // max(1, -(-l // 256)))))
+    acc = _lib.accum_dtype(qh.dtype)
+    qd, kd, vd = (torch.empty((bh, l, d), dtype=qh.dtype, device=dev) for _ in range(3))
+    od = torch.empty((bh, l, d), dtype=qh.dtype, device=dev)
+    dd = torch.empty((bh, l), dtype=acc, device=dev)
+    pin = torch.cuda.is_available()
+    oh = torch.empty((b, h, l, d), dtype=qh.dtype, pin_memory=pin)
+    dh = torch.empty((b, h, l, 1), dtype=acc, pin_memory=pin) if return_denominator else None
+    srcs = [t.reshape(bh, l, d) for t in (qh, kh, vh)]
+    of = oh.view(bh, l, d)
+    df = dh.view(bh, l) if dh is not None else None
+    lib = _lib.load()
+    with torch.cuda.device(dev):
+        cur = torch.cuda.current_stream(dev)
+        up, down = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+        # The fresh device buffers come from the compute stream's pool: order
+        # the uploads after the work already queued there. Chunks use disjoint
+        # slices, so nothing else orders one chunk's upload after another's use.
+        up.wait_stream(cur)
+        for c0 in range(0, bh, per):
+            c1 = min(bh, c0 + per)
+            with torch.cuda.stream(up):
+                for dst, src in zip((qd, kd, vd), srcs):
+                    dst[c0:c1].copy_(src[c0:c1], non_blocking=True)
+            cur.wait_stream(up)
+            rc = lib.afa_fwd(qd[c0].data_ptr(), kd[c0].data_ptr(), vd[c0].data_ptr(), od[c0].data_ptr(),
+                             dd[c0].data_ptr(), 1, c1 - c0, l, d, code, float(sink_omega), int(bool(causal)),
+                             int(valid_seq_len or 0), cur.cuda_stream)
+            _lib.check(rc, "afa_fwd")
+            down.wait_stream(cur)
+            with torch.cuda.stream(down):
+                of[c0:c1].copy_(od[c0:c1], non_blocking=True)
+                if df is not None:
+                    df[c0:c1].copy_(dd[c0:c1], non_blocking=True)
+        cur.wait_stream(down)
+        down.synchronize()
+    outs = (oh, dh) if return_denominator else (oh,)
+    if as_numpy:
+        outs = tuple(t.numpy() for t in outs)
+    return outs if return_denominator else outs[0]
+
+
 def _launch_fwd(q, k, v, sink_omega, causal, valid_seq_len, return_denominator):
+    if _is_host(q) and _is_host(k) and _is_host(v):
+        return _launch_fwd_host(q, k, v, sink_omega, causal, valid_seq_len, return_denominator)
     st = Staged(q, k, v)
     q, k, v = st.tensors
     if not (q.dtype == k.dtype == v.dtype):

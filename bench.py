@@ -292,7 +292,9 @@ def run_ring(args, rank, world, peaks, traffic):
 
 
 def run_ring_e2e(args, rank, world):
-    """Public API with host buffers: pinned host shards -> device -> ring -> host."""
+    """Public API with host buffers. N=1: pinned host Q/K/V go straight into
+    pallas_afa_forward, which returns the output in host memory; N>1: pinned
+    host shards -> device -> distributed_ring_afa -> host."""
     import torch
     import algebraic_intelligence_b200 as afa
     sets = ring_inputs(rank, world, 0)
@@ -302,12 +304,14 @@ def run_ring_e2e(args, rank, world):
     del sets
 
     def step(i, kt):
+        if world == 1:
+            # Host tensors straight into the public API, which streams them
+            # through the GPU in chunks, copies overlapping the kernels.
+            afa.pallas_afa_forward(host[0], host[1], host[2], causal=True)
+            return
         for d_, h_ in zip(dev, host):
             d_.copy_(h_, non_blocking=True)
-        if world == 1:
-            y = afa.pallas_afa_forward(dev[0], dev[1], dev[2], causal=True)
-        else:
-            y = afa.distributed_ring_afa(dev[0], dev[1], dev[2], causal=True, num_devices=world, layout="zigzag")
+        y = afa.distributed_ring_afa(dev[0], dev[1], dev[2], causal=True, num_devices=world, layout="zigzag")
         out_host.copy_(y, non_blocking=True)
 
     steps = max(2, min(args.steps, 5))

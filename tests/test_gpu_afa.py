@@ -338,3 +338,27 @@ def test_softmax_vjp_float16_and_numpy():
     want = orc.attention_vjp(xh.double().cpu().numpy(), gh.double().cpu().numpy(), 0.5)
     assert dxh.dtype == torch.float16
     np.testing.assert_allclose(dxh.double().cpu().numpy(), want, rtol=0.016, atol=0.016)
+
+
+# ---------------------------------------------------------------------------
+# Host inputs: the pipelined chunked path (copies overlapping kernels)
+# ---------------------------------------------------------------------------
+@pytest.mark.parametrize("shape,causal", [((2, 8, 1024, 128), True), ((1, 3, 700, 64), False), ((3, 2, 300, 128), True)])
+def test_host_inputs_match_device_path(shape, causal):
+    """pallas_afa_forward on pinned CPU tensors and on NumPy arrays gives the
+    device path's output bit for bit (the chunks run the same kernel on the same
+    rows), including d_total."""
+    g = torch.Generator(device="cuda").manual_seed(31)
+    q, k, v = (torch.randn(shape, generator=g, device="cuda").to(torch.bfloat16) for _ in range(3))
+    n = shape[2]
+    want, wden = afa.pallas_afa_forward(q, k, v, causal=causal, block_q=n, block_k=n, return_denominator=True)
+    qh, kh, vh = (t.cpu().pin_memory() for t in (q, k, v))
+    got, gden = afa.pallas_afa_forward(qh, kh, vh, causal=causal, block_q=n, block_k=n, return_denominator=True)
+    assert not got.is_cuda and got.dtype == torch.bfloat16
+    assert torch.equal(got, want.cpu()) and torch.equal(gden, wden.cpu())
+    qn, kn, vn = (t.float().cpu().numpy() for t in (q, k, v))
+    out_np = afa.pallas_afa_forward(qn, kn, vn, causal=causal, block_q=n, block_k=n)
+    assert isinstance(out_np, np.ndarray) and out_np.shape == shape
+    ref = afa.pallas_afa_forward(*(torch.as_tensor(a, device="cuda") for a in (qn, kn, vn)), causal=causal,
+                                 block_q=n, block_k=n)
+    assert np.array_equal(out_np, ref.cpu().numpy())
