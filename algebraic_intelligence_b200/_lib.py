@@ -46,6 +46,7 @@ SIGNATURES = {
     "algebraic_softmax_bwd": (_c_int, [_c_void_p, _c_void_p, _c_void_p, _c_ll, _c_int, _c_int, _c_double, _c_double,
                                        _c_void_p]),
     "afa_octic": (_c_int, [_c_void_p, _c_void_p, _c_ll, _c_int, _c_void_p]),
+    "afa_octic_bwd": (_c_int, [_c_void_p, _c_void_p, _c_void_p, _c_ll, _c_int, _c_void_p]),
     "afa_device_status": (_c_int, [_c_void_p, ctypes.POINTER(ctypes.c_int), _c_int]),
     "afa_selftest_bounded_wait": (_c_int, [_c_ll, _c_void_p]),
 }

@@ -9,7 +9,8 @@
   reference's custom VJP (attention.py:70-85) on the GPU.
 * ``algebraic_softmax_vjp(scores, g, sink_omega=0.5, eps=1e-5)`` -- that VJP as a
   plain function (the cotangent of the scores given the output cotangent g).
-* ``octic_kernel(x)`` -- src/attention.py:47-50: rho(x)^8 elementwise.
+* ``octic_kernel(x)`` -- src/attention.py:47-50: rho(x)^8 elementwise,
+  differentiable under torch autograd (its VJP, attention.py:38-44).
 """
 from __future__ import annotations
 
@@ -106,19 +107,49 @@ def algebraic_softmax_vjp(scores, g, sink_omega: float = 0.5, eps: float = 1e-5)
     return st.back(_softmax_bwd(x, gt, sink_omega, eps))
 
 
+def _octic_fwd(x):
+    y = torch.empty_like(x)
+    with torch.cuda.device(x.device):
+        rc = _lib.load().afa_octic(x.data_ptr(), y.data_ptr(), x.numel(), _lib.dtype_code(x.dtype),
+                                   _lib.stream_ptr(x.device))
+    _lib.check(rc, "octic_kernel")
+    return y
+
+
+class _Octic(torch.autograd.Function):
+    """octic_kernel with its custom VJP (attention.py:38-44)."""
+
+    @staticmethod
+    def forward(ctx, x):
+        ctx.save_for_backward(x)
+        return _octic_fwd(x)
+
+    @staticmethod
+    def backward(ctx, g):
+        (x,) = ctx.saved_tensors
+        g = g.to(x.dtype).contiguous()
+        dx = torch.empty_like(x)
+        with torch.cuda.device(x.device):
+            rc = _lib.load().afa_octic_bwd(x.data_ptr(), g.data_ptr(), dx.data_ptr(), x.numel(),
+                                           _lib.dtype_code(x.dtype), _lib.stream_ptr(x.device))
+        _lib.check(rc, "octic_kernel backward")
+        return dx
+
+
 def octic_kernel(x):
     """rho(x)^8 via three squarings after evaluating rho (src/attention.py:47-50).
 
     Evaluated in the accumulation dtype with the reference's cancellation-free
-    branch for negative x (attention.py:18-26), returned in x's dtype.
+    branch for negative x (attention.py:18-26), returned in x's dtype. For CUDA
+    tensors that require gradients, autograd applies the reference's VJP,
+    8 rsqrt(1 + x^2) rho(x)^8 (attention.py:38-44).
     """
     x = _as_array(x)
     host_checks_float(x)
+    if isinstance(x, torch.Tensor) and x.requires_grad:
+        if not x.is_cuda:
+            raise ValueError("a differentiable octic_kernel needs a CUDA tensor")
+        return _Octic.apply(x.contiguous())
     st = Staged(x)
     (xt,) = st.tensors
-    y = torch.empty_like(xt)
-    with torch.cuda.device(xt.device):
-        rc = _lib.load().afa_octic(xt.data_ptr(), y.data_ptr(), xt.numel(), _lib.dtype_code(xt.dtype),
-                                   _lib.stream_ptr(xt.device))
-    _lib.check(rc, "octic_kernel")
-    return st.back(y)
+    return st.back(_octic_fwd(xt))

@@ -279,6 +279,16 @@ int algebraic_softmax_bwd(const void* x, const void* g, void* dx, long long rows
   return AFA_OK;
 }
 
+int afa_octic_bwd(const void* x, const void* g, void* dx, long long n, int dtype, void* stream) {
+  if (dtype != AFA_F32 && dtype != AFA_BF16 && dtype != AFA_F16 && dtype != AFA_F64)
+    return fail(AFA_ERR_DTYPE, "expected a floating point array");
+  if (n < 0) return fail(AFA_ERR_INVALID, "negative element count");
+  if (n > 0 && (!x || !g || !dx)) return fail(AFA_ERR_INVALID, "x, g and dx must be non-null device pointers");
+  cudaError_t e = afa::launch_octic_bwd(x, g, dx, n, dtype, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "afa_octic_bwd launch");
+  return AFA_OK;
+}
+
 int afa_octic(const void* x, void* y, long long n, int dtype, void* stream) {
   if (dtype != AFA_F32 && dtype != AFA_BF16 && dtype != AFA_F16 && dtype != AFA_F64)
     return fail(AFA_ERR_DTYPE, "expected a floating point array");

@@ -59,6 +59,7 @@ cudaError_t launch_softmax(const void* x, void* y, long long rows, int cols, int
 cudaError_t launch_softmax_bwd(const void* x, const void* g, void* dx, long long rows, int cols, int dtype, double sink,
                                double eps, cudaStream_t stream);
 cudaError_t launch_octic(const void* x, void* y, long long n, int dtype, cudaStream_t stream);
+cudaError_t launch_octic_bwd(const void* x, const void* g, void* dx, long long n, int dtype, cudaStream_t stream);
 
 // Records `msg` as the calling thread's afa_last_error() and returns `code`.
 int set_last_error(int code, const char* msg);

@@ -18,7 +18,8 @@
 // are recomputed from x, so the backward reads x and g and writes dx.
 //
 // octic_kernel (attention.py:47-50): y = rho(x)^8 elementwise in the
-// accumulation dtype, returned in the input dtype.
+// accumulation dtype, returned in the input dtype; its VJP (attention.py:38-44)
+// dx = 8 r rho(x)^8 g with r = rsqrt(1 + x^2), returned in g's dtype.
 #include "afa_common.cuh"
 #include "afa_internal.h"
 
@@ -272,6 +273,27 @@ cudaError_t softmax_t(const void* x, void* y, long long rows, int cols, double s
 }
 
 template <typename T>
+__global__ void octic_bwd_kernel(const T* __restrict__ x, const T* __restrict__ g, T* __restrict__ dx, long long n) {
+  using A = typename AccOf<T>::type;
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const A xv = static_cast<A>(to_acc(x[i]));
+    const A r = rsqrt_acc<A>(fma(xv, xv, A(1)));
+    dx[i] = from_acc<T>(A(8) * r * octic_ref(xv) * static_cast<A>(to_acc(g[i])));
+  }
+}
+
+template <typename T>
+cudaError_t octic_bwd_t(const void* x, const void* g, void* dx, long long n, cudaStream_t stream) {
+  if (n == 0) return cudaSuccess;
+  const long long want = (n + 255) / 256;
+  const int blocks = static_cast<int>(want < 148 * 32 ? want : 148 * 32);
+  octic_bwd_kernel<T><<<blocks, 256, 0, stream>>>(static_cast<const T*>(x), static_cast<const T*>(g),
+                                                  static_cast<T*>(dx), n);
+  return cudaGetLastError();
+}
+
+template <typename T>
 cudaError_t octic_t(const void* x, void* y, long long n, cudaStream_t stream) {
   if (n == 0) return cudaSuccess;
   const long long want = (n + 255) / 256;
@@ -302,6 +324,16 @@ cudaError_t launch_softmax_bwd(const void* x, const void* g, void* dx, long long
     case kBF16: return softmax_bwd_t<__nv_bfloat16>(x, g, dx, rows, cols, sink, eps, stream);
     case kF16: return softmax_bwd_t<__half>(x, g, dx, rows, cols, sink, eps, stream);
     case kF64: return softmax_bwd_t<double>(x, g, dx, rows, cols, sink, eps, stream);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+cudaError_t launch_octic_bwd(const void* x, const void* g, void* dx, long long n, int dtype, cudaStream_t stream) {
+  switch (dtype) {
+    case kF32: return octic_bwd_t<float>(x, g, dx, n, stream);
+    case kBF16: return octic_bwd_t<__nv_bfloat16>(x, g, dx, n, stream);
+    case kF16: return octic_bwd_t<__half>(x, g, dx, n, stream);
+    case kF64: return octic_bwd_t<double>(x, g, dx, n, stream);
     default: return cudaErrorInvalidValue;
   }
 }

@@ -23,7 +23,7 @@
  *                            token over a KV cache (pallas_afa_forward with Lq=1)
  *   algebraic_softmax_fwd <- algebraic_softmax   (src/attention.py:88-91, :59-67)
  *   algebraic_softmax_bwd <- its custom VJP      (src/attention.py:70-85)
- *   afa_octic             <- octic_kernel        (src/attention.py:47-50) and
+ *   afa_octic(_bwd)       <- octic_kernel and its VJP (src/attention.py:38-50) and
  *                            _vmu_octic_kernel   (pallas_afa.py:32-49)
  *
  * Conventions
@@ -240,6 +240,8 @@ AFA_API int algebraic_softmax_fwd(const void* x, void* y, long long rows, int co
 
 /* octic_kernel (src/attention.py:47-50): y = rho(x)^8 elementwise, n elements. */
 AFA_API int afa_octic(const void* x, void* y, long long n, int dtype, void* stream);
+/* The VJP of octic_kernel (src/attention.py:38-44): dx = 8 r rho(x)^8 g, r = rsqrt(1 + x^2). */
+AFA_API int afa_octic_bwd(const void* x, const void* g, void* dx, long long n, int dtype, void* stream);
 
 /*
  * algebraic_softmax backward: the custom VJP of algebraic_softmax

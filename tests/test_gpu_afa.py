@@ -362,3 +362,18 @@ def test_host_inputs_match_device_path(shape, causal):
     ref = afa.pallas_afa_forward(*(torch.as_tensor(a, device="cuda") for a in (qn, kn, vn)), causal=causal,
                                  block_q=n, block_k=n)
     assert np.array_equal(out_np, ref.cpu().numpy())
+
+
+def test_octic_kernel_gradient():
+    """tests/test_attention.py:28-35: grad of sum(octic_kernel(x)) equals
+    8 rho(x)^8 / sqrt(1 + x^2) (rtol 2e-13 in float64), tails included."""
+    x = np.r_[np.linspace(-64, 64, 1001), -1e3, 1e3]
+    xt = torch.as_tensor(x, device="cuda").requires_grad_(True)
+    afa.octic_kernel(xt).sum().backward()
+    want = 8 * orc.octic(x) / np.sqrt(1 + x ** 2)
+    np.testing.assert_allclose(xt.grad.cpu().numpy(), want, rtol=2e-13)
+    x32 = torch.linspace(-8, 8, 4097, device="cuda", dtype=torch.float32).requires_grad_(True)
+    g = torch.randn(4097, device="cuda")
+    afa.octic_kernel(x32).backward(g)
+    want32 = 8 * orc.octic(x32.detach().double().cpu().numpy()) / np.sqrt(1 + x32.detach().double().cpu().numpy() ** 2)
+    np.testing.assert_allclose(x32.grad.double().cpu().numpy(), want32 * g.double().cpu().numpy(), rtol=2e-5, atol=1e-30)
