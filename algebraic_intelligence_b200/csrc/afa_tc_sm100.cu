@@ -628,6 +628,33 @@ __device__ __forceinline__ void red_add(float* p, float a) {
   asm volatile("red.global.add.f32 [%0], %1;" ::"l"(p), "f"(a) : "memory");
 }
 
+// Transposes NCH x NCH blocks of float4 chunks within groups of NCH lanes:
+// lane i of a group holds chunks j = 0..NCH-1 (v[4j..4j+3]) of its own row;
+// afterwards it holds chunk i of the group's rows 0..NCH-1 (slot k = row k).
+// log2(NCH) exchange stages: at stage m a lane swaps, with lane i^m, the
+// chunks whose index differs from its own index in bit m.
+template <int NCH>
+__device__ __forceinline__ void transpose_chunks(uint32_t (&v)[32], int i) {
+#pragma unroll
+  for (int m = NCH / 2; m >= 1; m >>= 1) {
+    const bool hi = (i & m) != 0;
+#pragma unroll
+    for (int j = 0; j < NCH; ++j) {
+      if (j & m) continue;  // pair (j, j | m)
+      const int jh = j | m;
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const uint32_t send = hi ? v[4 * j + e] : v[4 * jh + e];
+        const uint32_t got = __shfl_xor_sync(0xffffffffu, send, m);
+        if (hi)
+          v[4 * j + e] = got;
+        else
+          v[4 * jh + e] = got;
+      }
+    }
+  }
+}
+
 template <int HD>
 __global__ void __launch_bounds__(576, 1)
     afa_tc_sk_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
@@ -866,14 +893,24 @@ __global__ void __launch_bounds__(576, 1)
           tmem_ld16(o_tm, ov16);
         }
         tmem_ld_wait();
-        if (rloc < P.q.len) {
-          float* acc_row = static_cast<float*>(L.o_acc) + grow * HD + OC * g;
+        // Each thread holds OC contiguous columns of one row. Transposed in
+        // groups of NCH lanes, the lanes of a group then reduce NCH
+        // consecutive 16-byte chunks of one row per instruction: full 32-byte
+        // sectors, half the L2 reduction requests of one row per lane.
+        constexpr int NCH = OC / 4;
+        const int gi = lane % NCH;
+        transpose_chunks<NCH>(ov, gi);
+        const int grow0 = G.r0 + 128 * tile + sub * 32 + (lane / NCH) * NCH;  // the group's first row
+        const long long gbase = static_cast<long long>(sg.bh) * L.lq + P.q.row0;
 #pragma unroll
-          for (int w = 0; w < OC / 4; ++w)
-            red_add_v4(acc_row + 4 * w, __uint_as_float(ov[4 * w + 0]), __uint_as_float(ov[4 * w + 1]),
-                       __uint_as_float(ov[4 * w + 2]), __uint_as_float(ov[4 * w + 3]));
-          red_add(static_cast<float*>(L.d_acc) + grow, dsum[tile]);
+        for (int kr = 0; kr < NCH; ++kr) {
+          if (grow0 + kr < P.q.len) {
+            float* dst = static_cast<float*>(L.o_acc) + (gbase + grow0 + kr) * HD + OC * g + 4 * gi;
+            red_add_v4(dst, __uint_as_float(ov[4 * kr + 0]), __uint_as_float(ov[4 * kr + 1]),
+                       __uint_as_float(ov[4 * kr + 2]), __uint_as_float(ov[4 * kr + 3]));
+          }
         }
+        if (rloc < P.q.len) red_add(static_cast<float*>(L.d_acc) + grow, dsum[tile]);
       }
       // The O reads above are complete (wait::ld) before this warp's next
       // P arrival, which is what lets the MMA warp overwrite O.
