@@ -52,7 +52,6 @@ struct TcCfg {
   static constexpr int kTmaWarp = 16;
   static constexpr int kMmaWarp = 17;
   static constexpr int kThreads = 18 * 32;
-  static constexpr int BM = 128;
   static constexpr int BN = 128;
   static constexpr int KSUB = HD / 64;             // 64-element (128 B) column blocks
   static constexpr int SUB_BYTES = 128 * 128;      // 128 rows x 128 B
@@ -159,6 +158,33 @@ __device__ __forceinline__ float map_chunk(const uint32_t (&sv)[32], uint32_t (&
     pk[e >> 1] = pack_bf16x2(p.x, p.y);
   }
   return acc.x + acc.y;
+}
+
+// Transposes NCH x NCH blocks of float4 chunks within groups of NCH lanes:
+// lane i of a group holds chunks j = 0..NCH-1 (v[4j..4j+3]) of its own row;
+// afterwards it holds chunk i of the group's rows 0..NCH-1 (slot k = row k).
+// log2(NCH) exchange stages: at stage m a lane swaps, with lane i^m, the
+// chunks whose index differs from its own index in bit m.
+template <int NCH>
+__device__ __forceinline__ void transpose_chunks(uint32_t (&v)[32], int i) {
+#pragma unroll
+  for (int m = NCH / 2; m >= 1; m >>= 1) {
+    const bool hi = (i & m) != 0;
+#pragma unroll
+    for (int j = 0; j < NCH; ++j) {
+      if (j & m) continue;  // pair (j, j | m)
+      const int jh = j | m;
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const uint32_t send = hi ? v[4 * j + e] : v[4 * jh + e];
+        const uint32_t got = __shfl_xor_sync(0xffffffffu, send, m);
+        if (hi)
+          v[4 * j + e] = got;
+        else
+          v[4 * jh + e] = got;
+      }
+    }
+  }
 }
 
 template <int HD>
@@ -428,7 +454,6 @@ __global__ void __launch_bounds__(576, 1)
       const int rloc = r0 + 128 * tile + row;
       const bool row_ok = rloc < P.q.len;
       const long long grow = static_cast<long long>(bh) * L.lq + P.q.row0 + rloc;
-      float* acc_row = fin && !add_prev ? nullptr : static_cast<float*>(L.o_acc) + grow * HD + OC * g;
       const float dprev = (row_ok && add_prev) ? static_cast<const float*>(L.d_acc)[grow] : 0.f;
       const float drow = drow_tile + dprev;
       const float denom = drow + L.sink;
@@ -448,21 +473,32 @@ __global__ void __launch_bounds__(576, 1)
 #pragma unroll
         for (int e = 0; e < 32; ++e) ov[e] = 0u;
       }
-      float x[OC];
-#pragma unroll
-      for (int e = 0; e < OC; ++e) x[e] = __uint_as_float(ov[e]);
-      if (row_ok && add_prev) {
-        const float4* src = reinterpret_cast<const float4*>(acc_row);
-#pragma unroll
-        for (int w = 0; w < OC / 4; ++w) {
-          const float4 y = src[w];
-          x[4 * w + 0] += y.x;
-          x[4 * w + 1] += y.y;
-          x[4 * w + 2] += y.z;
-          x[4 * w + 3] += y.w;
-        }
-      }
+      constexpr int NCH = OC / 4;  // 16-byte chunks per row and warpgroup
+      const int gi = lane % NCH;
+      const int grow0 = r0 + 128 * tile + sub * 32 + (lane / NCH) * NCH;  // first row of the lane's group
+      const long long gbase = static_cast<long long>(bh) * L.lq + P.q.row0;
       if (fin) {
+        if (add_prev) {
+          // The previous hops' rows are read transposed (NCH consecutive
+          // chunks of one row per group and instruction, not one chunk of 32
+          // rows), then the transpose is undone for the per-row epilogue.
+          transpose_chunks<NCH>(ov, gi);
+#pragma unroll
+          for (int kr = 0; kr < NCH; ++kr) {
+            if (grow0 + kr < P.q.len) {
+              const float4 y = *reinterpret_cast<const float4*>(static_cast<const float*>(L.o_acc) +
+                                                                (gbase + grow0 + kr) * HD + OC * g + 4 * gi);
+              ov[4 * kr + 0] = __float_as_uint(__uint_as_float(ov[4 * kr + 0]) + y.x);
+              ov[4 * kr + 1] = __float_as_uint(__uint_as_float(ov[4 * kr + 1]) + y.y);
+              ov[4 * kr + 2] = __float_as_uint(__uint_as_float(ov[4 * kr + 2]) + y.z);
+              ov[4 * kr + 3] = __float_as_uint(__uint_as_float(ov[4 * kr + 3]) + y.w);
+            }
+          }
+          transpose_chunks<NCH>(ov, gi);
+        }
+        float x[OC];
+#pragma unroll
+        for (int e = 0; e < OC; ++e) x[e] = __uint_as_float(ov[e]);
         uint4 pk[OC / 8];
 #pragma unroll
         for (int w = 0; w < OC / 8; ++w) {
@@ -486,10 +522,32 @@ __global__ void __launch_bounds__(576, 1)
 #pragma unroll
           for (int w = 0; w < OC / 8; ++w) dst[w] = pk[w];
         }
-      } else if (row_ok) {
-        float4* dst = reinterpret_cast<float4*>(acc_row);
+      } else {
+        // Raw accumulator rows (store, or add the previous hops'): transposed
+        // so the lanes of a group move NCH consecutive 16-byte chunks of one
+        // row per instruction, rather than one chunk of 32 rows.
+        // All loads are issued before the first store, which the compiler
+        // could not move them past.
+        transpose_chunks<NCH>(ov, gi);
+        float* const acc0 = static_cast<float*>(L.o_acc) + (gbase + grow0) * HD + OC * g + 4 * gi;
+        if (add_prev) {
 #pragma unroll
-        for (int w = 0; w < OC / 4; ++w) dst[w] = make_float4(x[4 * w + 0], x[4 * w + 1], x[4 * w + 2], x[4 * w + 3]);
+          for (int kr = 0; kr < NCH; ++kr) {
+            if (grow0 + kr < P.q.len) {
+              const float4 y = *reinterpret_cast<const float4*>(acc0 + kr * HD);
+              ov[4 * kr + 0] = __float_as_uint(__uint_as_float(ov[4 * kr + 0]) + y.x);
+              ov[4 * kr + 1] = __float_as_uint(__uint_as_float(ov[4 * kr + 1]) + y.y);
+              ov[4 * kr + 2] = __float_as_uint(__uint_as_float(ov[4 * kr + 2]) + y.z);
+              ov[4 * kr + 3] = __float_as_uint(__uint_as_float(ov[4 * kr + 3]) + y.w);
+            }
+          }
+        }
+#pragma unroll
+        for (int kr = 0; kr < NCH; ++kr) {
+          if (grow0 + kr < P.q.len)
+            *reinterpret_cast<uint4*>(acc0 + kr * HD) =
+                make_uint4(ov[4 * kr + 0], ov[4 * kr + 1], ov[4 * kr + 2], ov[4 * kr + 3]);
+        }
       }
       // d_acc / d_total: one writer per row (warpgroup 0); the others only
       // read d_acc above, in kAccumFinal, where nothing writes it.
@@ -626,33 +684,6 @@ __device__ __forceinline__ void red_add_v4(float* p, float a, float b, float c, 
 
 __device__ __forceinline__ void red_add(float* p, float a) {
   asm volatile("red.global.add.f32 [%0], %1;" ::"l"(p), "f"(a) : "memory");
-}
-
-// Transposes NCH x NCH blocks of float4 chunks within groups of NCH lanes:
-// lane i of a group holds chunks j = 0..NCH-1 (v[4j..4j+3]) of its own row;
-// afterwards it holds chunk i of the group's rows 0..NCH-1 (slot k = row k).
-// log2(NCH) exchange stages: at stage m a lane swaps, with lane i^m, the
-// chunks whose index differs from its own index in bit m.
-template <int NCH>
-__device__ __forceinline__ void transpose_chunks(uint32_t (&v)[32], int i) {
-#pragma unroll
-  for (int m = NCH / 2; m >= 1; m >>= 1) {
-    const bool hi = (i & m) != 0;
-#pragma unroll
-    for (int j = 0; j < NCH; ++j) {
-      if (j & m) continue;  // pair (j, j | m)
-      const int jh = j | m;
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const uint32_t send = hi ? v[4 * j + e] : v[4 * jh + e];
-        const uint32_t got = __shfl_xor_sync(0xffffffffu, send, m);
-        if (hi)
-          v[4 * j + e] = got;
-        else
-          v[4 * jh + e] = got;
-      }
-    }
-  }
 }
 
 template <int HD>

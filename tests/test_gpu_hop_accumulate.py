@@ -137,3 +137,31 @@ def test_split_finalize_matches_oracle():
     want = orc.afa(qn, kn, vn, sink=SINK, causal=False)
     got = out[:, heads].double().cpu().numpy()
     assert float(np.max(np.abs(got - want)) / np.max(np.abs(want))) <= 2e-2
+
+
+def test_large_hop_non_persistent_epilogues():
+    """Hops with more than 1024 query pairs per head take the non-persistent
+    kernel in ACCUMULATE and FINALIZE too, whose epilogues read (and write) the
+    fp32 accumulator rows in groups of consecutive rows. Two problems split the
+    rows off any tile or group boundary, so groups straddle a problem's end."""
+    h, lq, lk, d = 1, 263000, 512, 128
+    split = 131085
+    problems = [(0, split, 0, [(0, lk, 0)]), (split, lq - split, 0, [(0, lk, 0)])]
+    q, k, v = _inputs(h, lq, lk, d, seed=31)
+    ref_o, ref_s = _store(q, k, v, problems, False)
+    g = torch.Generator(device="cuda").manual_seed(8)
+    prev_o = torch.randn(ref_o.shape, generator=g, device="cuda") * ref_o.abs().max()
+    prev_s = torch.rand(ref_s.shape, generator=g, device="cuda") * ref_s.max()
+    o, s = prev_o.clone(), prev_s.clone()
+    hop_forward(q, k, v, problems, False, _lib.AFA_HOP_ACCUMULATE, o_acc=o, d_acc=s, sink_omega=SINK)
+    torch.cuda.synchronize()
+    assert _rel(o, prev_o + ref_o) <= TOL_ACC
+    assert _rel(s, prev_s + ref_s) <= TOL_ACC
+    out = torch.full_like(q, float("nan"))
+    hop_forward(q, k, v, problems, False, _lib.AFA_HOP_FINALIZE, o_acc=prev_o.clone(), d_acc=prev_s.clone(),
+                out=out, sink_omega=SINK)
+    torch.cuda.synchronize()
+    want = (prev_o + ref_o) / (prev_s + ref_s + SINK)[..., None]
+    assert torch.isfinite(out.float()).all()
+    assert _rel(out, want) <= TOL_BF16
+    assert _lib.device_status(q.device) == 0
