@@ -268,7 +268,7 @@ __global__ void __launch_bounds__(576, 1)
   if (threadIdx.x == 0) {
     for (int i = 0; i < 2; ++i) {
       mbar_init(s_full + i, 1);
-      mbar_init(p_full + i, 16);  // one elected arrive per octic warp
+      mbar_init(p_full + i, 8);  // one elected arrive per octic warp of the tile
       mbar_init(o_full + i, 1);
     }
     mbar_init(drain, 1);
@@ -382,42 +382,51 @@ __global__ void __launch_bounds__(576, 1)
     }
   } else {
     // --------------------------------------------------- octic map + epilogue
-    const int g = warp >> 2;           // warpgroup: key columns [32g, 32g+32)
+    // Map: warps 0-7 take query tile 0, warps 8-15 tile 1, so one tile's map
+    // runs while the tensor core works on the other's P.V and next scores, and
+    // the TMEM load/store latency of one overlaps the other's MUFU work. Warp
+    // (mt, h, sub) maps key columns [64h, 64h+64) of TMEM lane quarter sub.
+    // Epilogue: warpgroup g = warp / 4 takes O columns [OC g, OC g + OC) of
+    // both tiles.
+    const int g = warp >> 2;
     const int sub = warp & 3;          // TMEM lane quarter
+    const int mt = warp >> 3;          // query tile this warp maps
+    const int mh = (warp >> 2) & 1;    // its half of the key columns
     const int row = sub * 32 + lane;
     const uint32_t lane_off = static_cast<uint32_t>(sub * 32) << 16;
     const float scale = L.scale;
-    float dsum[2] = {0.f, 0.f};
+    float dsum = 0.f;
     bool ok = true;
-    for (int t = 0; t < n1 && ok; ++t) {
+    const int nmap = mt ? n1 : n0;
+    for (int t = 0; t < nmap && ok; ++t) {
       const KvTile kt = kv_tile(P, cnt1[0], t);
-#pragma unroll
-      for (int tile = 0; tile < 2; ++tile) {
-        if (tile == 0 && t >= n0) continue;
-        ok = mbar_wait(s_full + tile, t & 1, L.status, kDevTimeoutSoftmax);
-        ok = __all_sync(0xffffffffu, ok);
-        if (!ok) break;
-        tc_fence_after();
-        const int qfirst = P.q.pos0 + r0 + 128 * tile;
-        const int qpos = qfirst + row;
-        const bool need_mask = kt.lim < 128 || (L.causal && kt.pos + 127 > qfirst);
-        const uint32_t s_tm = tmem + C::s_col(tile) + lane_off + 32 * g;
+      ok = mbar_wait(s_full + mt, t & 1, L.status, kDevTimeoutSoftmax);
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok) break;
+      tc_fence_after();
+      const int qfirst = P.q.pos0 + r0 + 128 * mt;
+      const int qpos = qfirst + row;
+      const bool need_mask = kt.lim < 128 || (L.causal && kt.pos + 127 > qfirst);
+#pragma unroll 1
+      for (int c = 0; c < 2; ++c) {
+        const int key0 = 64 * mh + 32 * c;
+        const uint32_t s_tm = tmem + C::s_col(mt) + lane_off + key0;
         uint32_t sv[32];
         uint32_t pk[16];
         tmem_ld32(s_tm, sv);
         tmem_ld_wait();
-        const float part = need_mask ? map_chunk<true>(sv, pk, scale, 32 * g, kt.lim, L.causal, kt.pos, qpos)
-                                     : map_chunk<false>(sv, pk, scale, 32 * g, kt.lim, L.causal, kt.pos, qpos);
+        const float part = need_mask ? map_chunk<true>(sv, pk, scale, key0, kt.lim, L.causal, kt.pos, qpos)
+                                     : map_chunk<false>(sv, pk, scale, key0, kt.lim, L.causal, kt.pos, qpos);
         // P of these 32 keys -> the first 16 of the 32 columns just read.
         tmem_st16(s_tm, pk);
-        // Every lane's P stores are complete (wait::st) and ordered before the
-        // warp's single arrive.
-        tmem_st_wait();
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(p_full + tile);
-        dsum[tile] += part;
+        dsum += part;
       }
+      // Every lane's P stores are complete (wait::st) and ordered before the
+      // warp's single arrive.
+      tmem_st_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(p_full + mt);
     }
     bool have_o[2] = {false, false};
 #pragma unroll
@@ -428,10 +437,10 @@ __global__ void __launch_bounds__(576, 1)
         ok = __all_sync(0xffffffffu, ok);
         have_o[tile] = ok;
       }
-      red[(tile * 4 + g) * 128 + row] = dsum[tile];
+      if (tile == mt) red[(tile * 2 + mh) * 128 + row] = dsum;
     }
     tc_fence_after();
-    // The four column partials of every row meet here (fixed order g = 0..3).
+    // The two column-half partials of every row meet here (fixed order).
     asm volatile("bar.sync 1, %0;" ::"r"(C::kOcticWarps * 32) : "memory");
 
     const bool fin = L.mode == kFinal || L.mode == kAccumFinal;
@@ -449,8 +458,7 @@ __global__ void __launch_bounds__(576, 1)
                        (r0 + 128 * (tile + 1) <= P.q.len || P.q.row0 + P.q.len == L.lq);
 #pragma unroll
     for (int tile = 0; tile < 2; ++tile) {
-      const float drow_tile = red[(tile * 4 + 0) * 128 + row] + red[(tile * 4 + 1) * 128 + row] +
-                              red[(tile * 4 + 2) * 128 + row] + red[(tile * 4 + 3) * 128 + row];
+      const float drow_tile = red[(tile * 2 + 0) * 128 + row] + red[(tile * 2 + 1) * 128 + row];
       const int rloc = r0 + 128 * tile + row;
       const bool row_ok = rloc < P.q.len;
       const long long grow = static_cast<long long>(bh) * L.lq + P.q.row0 + rloc;
