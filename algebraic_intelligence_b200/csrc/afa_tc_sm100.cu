@@ -727,7 +727,7 @@ __global__ void __launch_bounds__(576, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(s_full + i, 1);
-      mbar_init(p_full + i, 16);
+      mbar_init(p_full + i, 8);  // one elected arrive per octic warp of the tile
       mbar_init(o_full + i, 1);
     }
     mbar_init(drain, 1);
@@ -867,89 +867,92 @@ __global__ void __launch_bounds__(576, 1)
     }
   } else {
     // ------------------------------------- octic map + accumulate epilogue
-    const int g = warp >> 2;
+    // Warps 0-7 map query tile 0 and warps 8-15 tile 1 (as in the
+    // non-persistent kernel); warp (mt, mh, sub) maps key columns
+    // [64 mh, 64 mh + 64) and, after each piece, adds O columns
+    // [HD/2 mh, HD/2 mh + HD/2) of its own tile, TMEM lane quarter sub. Reading
+    // only its own tile's O keeps the overwrite of O by the next piece's first
+    // P.V behind this warp's own next P arrival.
     const int sub = warp & 3;
+    const int mt = warp >> 3;
+    const int mh = (warp >> 2) & 1;
     const int row = sub * 32 + lane;
     const uint32_t lane_off = static_cast<uint32_t>(sub * 32) << 16;
     const float scale = L.scale;
-    constexpr int OC = HD / 4;
     SkSeg sg;
-    int sc[2] = {0, 0}, oc[2] = {0, 0};
+    int sc = 0, oc = 0;
     bool ok = true;
     while (ok && walk.next(sg)) {
       const PairGeom G = pair_geom(L, S.pair_of[sg.item]);
       const Problem& P = L.prob[G.pi];
       const int e0 = sg.t1 < G.n0 ? sg.t1 : G.n0;
-      float dsum[2] = {0.f, 0.f};
-      for (int t = sg.t0; t < sg.t1 && ok; ++t) {
+      const int tend = mt ? sg.t1 : e0;  // this warp's tile: key tiles [sg.t0, tend)
+      float dsum = 0.f;
+      for (int t = sg.t0; t < tend && ok; ++t) {
         const KvTile kt = kv_tile(P, G.cnt1_0, t);
-#pragma unroll
-        for (int tile = 0; tile < 2; ++tile) {
-          if (tile == 0 && t >= e0) continue;
-          ok = mbar_wait(s_full + tile, sc[tile] & 1, L.status, kDevTimeoutSoftmax);
-          ++sc[tile];
-          ok = __all_sync(0xffffffffu, ok);
-          if (!ok) break;
-          tc_fence_after();
-          const int qfirst = P.q.pos0 + G.r0 + 128 * tile;
-          const int qpos = qfirst + row;
-          const bool need_mask = kt.lim < 128 || (L.causal && kt.pos + 127 > qfirst);
-          const uint32_t s_tm = tmem + C::s_col(tile) + lane_off + 32 * g;
+        ok = mbar_wait(s_full + mt, sc & 1, L.status, kDevTimeoutSoftmax);
+        ++sc;
+        ok = __all_sync(0xffffffffu, ok);
+        if (!ok) break;
+        tc_fence_after();
+        const int qfirst = P.q.pos0 + G.r0 + 128 * mt;
+        const int qpos = qfirst + row;
+        const bool need_mask = kt.lim < 128 || (L.causal && kt.pos + 127 > qfirst);
+#pragma unroll 1
+        for (int c = 0; c < 2; ++c) {
+          const int key0 = 64 * mh + 32 * c;
+          const uint32_t s_tm = tmem + C::s_col(mt) + lane_off + key0;
           uint32_t sv[32];
           uint32_t pk[16];
           tmem_ld32(s_tm, sv);
           tmem_ld_wait();
-          const float part = need_mask ? map_chunk<true>(sv, pk, scale, 32 * g, kt.lim, L.causal, kt.pos, qpos)
-                                       : map_chunk<false>(sv, pk, scale, 32 * g, kt.lim, L.causal, kt.pos, qpos);
+          const float part = need_mask ? map_chunk<true>(sv, pk, scale, key0, kt.lim, L.causal, kt.pos, qpos)
+                                       : map_chunk<false>(sv, pk, scale, key0, kt.lim, L.causal, kt.pos, qpos);
           tmem_st16(s_tm, pk);
-          tmem_st_wait();
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(p_full + tile);
-          dsum[tile] += part;
+          dsum += part;
         }
+        tmem_st_wait();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(p_full + mt);
       }
-      // Add this piece into the accumulators. Every warpgroup adds its own
-      // columns of O and its own partial row sum (four adds per row).
-#pragma unroll
-      for (int tile = 0; tile < 2; ++tile) {
-        if (tile == 0 && sg.t0 >= e0) continue;  // tile 0 had no key tiles in this piece
-        if (!ok) break;
-        ok = mbar_wait(o_full + tile, oc[tile] & 1, L.status, kDevTimeoutEpilogue);
-        ++oc[tile];
+      // Add this piece into the accumulators: this warp's O columns of its
+      // tile and its partial row sum (two adds per row).
+      if (ok && sg.t0 < tend) {
+        ok = mbar_wait(o_full + mt, oc & 1, L.status, kDevTimeoutEpilogue);
+        ++oc;
         ok = __all_sync(0xffffffffu, ok);
-        if (!ok) break;
-        tc_fence_after();
-        const int rloc = G.r0 + 128 * tile + row;
-        const long long grow = static_cast<long long>(sg.bh) * L.lq + P.q.row0 + rloc;
-        uint32_t ov[32];
-        __syncwarp();  // tcgen05.ld is warp-collective
-        const uint32_t o_tm = tmem + C::o_col(tile) + lane_off + OC * g;
-        if constexpr (OC == 32) {
-          tmem_ld32(o_tm, ov);
-        } else {
-          uint32_t (&ov16)[16] = *reinterpret_cast<uint32_t(*)[16]>(ov);
-          tmem_ld16(o_tm, ov16);
-        }
-        tmem_ld_wait();
-        // Each thread holds OC contiguous columns of one row. Transposed in
-        // groups of NCH lanes, the lanes of a group then reduce NCH
-        // consecutive 16-byte chunks of one row per instruction: full 32-byte
-        // sectors, half the L2 reduction requests of one row per lane.
-        constexpr int NCH = OC / 4;
-        const int gi = lane % NCH;
-        transpose_chunks<NCH>(ov, gi);
-        const int grow0 = G.r0 + 128 * tile + sub * 32 + (lane / NCH) * NCH;  // the group's first row
-        const long long gbase = static_cast<long long>(sg.bh) * L.lq + P.q.row0;
+        if (ok) {
+          tc_fence_after();
+          const int rloc = G.r0 + 128 * mt + row;
+          const long long grow = static_cast<long long>(sg.bh) * L.lq + P.q.row0 + rloc;
+          // Each thread holds 32 contiguous columns of one row per chunk.
+          // Transposed in groups of 8 lanes, the lanes of a group then reduce
+          // 8 consecutive 16-byte chunks of one row per instruction: full
+          // 32-byte sectors, 128 contiguous bytes per row.
+          constexpr int NCH = 8;
+          const int gi = lane % NCH;
+          const int grow0 = G.r0 + 128 * mt + sub * 32 + (lane / NCH) * NCH;  // the group's first row
+          const long long gbase = static_cast<long long>(sg.bh) * L.lq + P.q.row0;
+#pragma unroll 1
+          for (int c = 0; c < HD / 64; ++c) {
+            const int col0 = (HD / 2) * mh + 32 * c;
+            uint32_t ov[32];
+            __syncwarp();  // tcgen05.ld is warp-collective
+            tmem_ld32(tmem + C::o_col(mt) + lane_off + col0, ov);
+            tmem_ld_wait();
+            transpose_chunks<NCH>(ov, gi);
 #pragma unroll
-        for (int kr = 0; kr < NCH; ++kr) {
-          if (grow0 + kr < P.q.len) {
-            float* dst = static_cast<float*>(L.o_acc) + (gbase + grow0 + kr) * HD + OC * g + 4 * gi;
-            red_add_v4(dst, __uint_as_float(ov[4 * kr + 0]), __uint_as_float(ov[4 * kr + 1]),
-                       __uint_as_float(ov[4 * kr + 2]), __uint_as_float(ov[4 * kr + 3]));
+            for (int kr = 0; kr < NCH; ++kr) {
+              if (grow0 + kr < P.q.len) {
+                float* dst = static_cast<float*>(L.o_acc) + (gbase + grow0 + kr) * HD + col0 + 4 * gi;
+                red_add_v4(dst, __uint_as_float(ov[4 * kr + 0]), __uint_as_float(ov[4 * kr + 1]),
+                           __uint_as_float(ov[4 * kr + 2]), __uint_as_float(ov[4 * kr + 3]));
+              }
+            }
           }
+          if (rloc < P.q.len) red_add(static_cast<float*>(L.d_acc) + grow, dsum);
         }
-        if (rloc < P.q.len) red_add(static_cast<float*>(L.d_acc) + grow, dsum[tile]);
       }
       // The O reads above are complete (wait::ld) before this warp's next
       // P arrival, which is what lets the MMA warp overwrite O.
