@@ -109,6 +109,23 @@ __global__ void __launch_bounds__(256) ago_rotate_kernel(const __grid_constant__
     const int pos = static_cast<int>((row / a.inner) % a.seq_len);
     const long long e0 = row * (2LL * a.pairs) + 2LL * p0;  // first element
     const long long t0 = static_cast<long long>(pos) * a.pairs + p0;
+    // V == 4: 16-byte chunks (the host picks it only for 16-byte-aligned
+    // rows); V == 1: element accesses. Both tensors' chunks are loaded before
+    // either is stored (the compiler may not move a load of k past a store to
+    // qo), which doubles the bytes each thread has in flight.
+    constexpr int N16 = V == 4 ? static_cast<int>(sizeof(T)) * 2 * V / 16 : 0;
+    alignas(16) T in[2][2 * V];
+#pragma unroll
+    for (int t = 0; t < 2; ++t) {
+      const T* x = static_cast<const T*>(t ? a.k : a.q) + e0;
+      if constexpr (N16 > 0) {
+#pragma unroll
+        for (int i = 0; i < N16; ++i) reinterpret_cast<uint4*>(in[t])[i] = reinterpret_cast<const uint4*>(x)[i];
+      } else {
+#pragma unroll
+        for (int i = 0; i < 2 * V; ++i) in[t][i] = x[i];
+      }
+    }
     A cc[V], ss[V];
 #pragma unroll
     for (int v = 0; v < V; ++v) {
@@ -117,23 +134,11 @@ __global__ void __launch_bounds__(256) ago_rotate_kernel(const __grid_constant__
     }
 #pragma unroll
     for (int t = 0; t < 2; ++t) {
-      const T* x = static_cast<const T*>(t ? a.k : a.q) + e0;
       T* y = static_cast<T*>(t ? a.ko : a.qo) + e0;
-      // V == 4: 16-byte chunks (the host picks it only for 16-byte-aligned
-      // rows); V == 1: element accesses.
-      constexpr int N16 = V == 4 ? static_cast<int>(sizeof(T)) * 2 * V / 16 : 0;
-      alignas(16) T in[2 * V];
       alignas(16) T out[2 * V];
-      if constexpr (N16 > 0) {
-#pragma unroll
-        for (int i = 0; i < N16; ++i) reinterpret_cast<uint4*>(in)[i] = reinterpret_cast<const uint4*>(x)[i];
-      } else {
-#pragma unroll
-        for (int i = 0; i < 2 * V; ++i) in[i] = x[i];
-      }
 #pragma unroll
       for (int v = 0; v < V; ++v) {
-        const A x0 = static_cast<A>(to_acc(in[2 * v])), x1 = static_cast<A>(to_acc(in[2 * v + 1]));
+        const A x0 = static_cast<A>(to_acc(in[t][2 * v])), x1 = static_cast<A>(to_acc(in[t][2 * v + 1]));
         out[2 * v] = from_acc<T>(cc[v] * x0 - ss[v] * x1);
         out[2 * v + 1] = from_acc<T>(ss[v] * x0 + cc[v] * x1);
       }
