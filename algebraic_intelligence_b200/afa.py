@@ -58,15 +58,34 @@ def _is_host(a) -> bool:
     return isinstance(a, np.ndarray) or (isinstance(a, torch.Tensor) and not a.is_cuda)
 
 
+def _host_chunks(bh, per):
+    """(start, end) ranges of the (batch x heads) chunks of a host-input forward.
+
+    Middle chunks hold `per` heads. The first and the last hold about half as
+    many: the first chunk's upload and the last chunk's download are the only
+    transfers no kernel overlaps.
+    """
+    edge = max(1, per // 2)
+    first = min(bh, edge)
+    last = min(bh - first, edge)
+    bounds = [0, first]
+    while bounds[-1] < bh - last:
+        bounds.append(min(bounds[-1] + per, bh - last))
+    if last:
+        bounds.append(bh)
+    return list(zip(bounds[:-1], bounds[1:]))
+
+
 def _launch_fwd_host(q, k, v, sink_omega, causal, valid_seq_len, return_denominator):
     """Forward of host arrays, pipelined over chunks of (batch x heads).
 
     Chunk c's H2D copies run on an upload stream while chunk c-1 computes, and
     chunk c's output copies back on a download stream while chunk c+1
     computes, so PCIe traffic and the kernels overlap (the copy engines carry
-    the transfers; from pinned memory they are fully asynchronous). Chunks hold
-    about two SM-waves of query pairs. Returns host arrays of the input kind
-    once the results are in host memory.
+    the transfers; from pinned memory they are fully asynchronous). Middle
+    chunks hold about two SM-waves of query pairs, the first and last about
+    half that (``_host_chunks``). Returns host arrays of the input kind once the
+    results are in host memory.
     """
     as_numpy = isinstance(q, np.ndarray)
     qh, kh, vh = (torch.from_numpy(np.ascontiguousarray(a)) if isinstance(a, np.ndarray) else a.contiguous()
@@ -99,8 +118,7 @@ def _launch_fwd_host(q, k, v, sink_omega, causal, valid_seq_len, return_denomina
         # the uploads after the work already queued there. Chunks use disjoint
         # slices, so nothing else orders one chunk's upload after another's use.
         up.wait_stream(cur)
-        for c0 in range(0, bh, per):
-            c1 = min(bh, c0 + per)
+        for c0, c1 in _host_chunks(bh, per):
             with torch.cuda.stream(up):
                 for dst, src in zip((qd, kd, vd), srcs):
                     dst[c0:c1].copy_(src[c0:c1], non_blocking=True)

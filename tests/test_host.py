@@ -300,3 +300,17 @@ def test_ring_exchange_protocol_over_gloo(world, causal):
         assert seen == want
         pulls = [(h.src, i % 2) for i, h in enumerate(hops) if i > 0 and h.problems]
         assert log == [e for _ in range(3) for e in [("pull", s, slot) for s, slot in pulls] + [("end",)]]
+
+
+@pytest.mark.parametrize("bh,per", [(16, 2), (64, 19), (1, 1), (2, 2), (3, 2), (5, 1), (7, 4), (4, 8), (16, 16),
+                                    (100, 7)])
+def test_host_chunks_cover_every_head_once(bh, per):
+    """The host-input forward's chunks tile (batch x heads) in order, middle
+    chunks at most `per`, the first and last at most about per / 2."""
+    from algebraic_intelligence_b200.afa import _host_chunks
+    ch = _host_chunks(bh, per)
+    assert [i for a, b in ch for i in range(a, b)] == list(range(bh))
+    assert all(0 < b - a <= per for a, b in ch)
+    edge = max(1, per // 2)
+    if bh > edge:
+        assert ch[0][1] - ch[0][0] == edge
