@@ -56,13 +56,19 @@ struct TcCfg {
   static constexpr int KSUB = HD / 64;             // 64-element (128 B) column blocks
   static constexpr int SUB_BYTES = 128 * 128;      // 128 rows x 128 B
   static constexpr int TILE_BYTES = KSUB * SUB_BYTES;
-  static constexpr int NSLOT = (HD == 128) ? 4 : 8;
+  static constexpr int NSLOT = (HD == 128) ? 5 : 8;
   static constexpr int Q_OFF = 0;
   static constexpr int KV_OFF = 2 * TILE_BYTES;
   static constexpr int BAR_OFF = KV_OFF + NSLOT * TILE_BYTES;
   static constexpr int NBAR = 1 + 2 * NSLOT + 2 + 2 + 2 + 1;
-  static constexpr int RED_OFF = BAR_OFF + NBAR * 8 + 16;  // fp32 row-sum partials [tile][warpgroup][row]
-  static constexpr int SMEM_BYTES = RED_OFF + 2 * 4 * 128 * 4 + 1024;
+  static constexpr int XBAR_OFF = BAR_OFF + NBAR * 8;  // one more barrier (the stream-K kernel's q_empty)
+  // fp32 row-sum partials [tile][column half][row] of the epilogue, in K/V
+  // ring slot 2 (idle once every MMA has finished; slots 0-1 stage the output
+  // tiles).
+  static constexpr int RED_OFF = KV_OFF + 2 * TILE_BYTES;
+  static constexpr int SMEM_BYTES = XBAR_OFF + 16 + 1024;
+  static_assert(NSLOT >= 3 && 2 * 2 * 128 * 4 <= TILE_BYTES, "row-sum partials fit in ring slot 2");
+  static_assert(SMEM_BYTES <= 227 * 1024, "shared memory per CTA");
   static constexpr uint32_t TMEM_COLS = 512;
   __device__ static constexpr uint32_t s_col(int i) { return static_cast<uint32_t>(i) * 128u; }
   __device__ static constexpr uint32_t o_col(int i) { return 256u + static_cast<uint32_t>(i) * HD; }
@@ -437,8 +443,9 @@ __global__ void __launch_bounds__(576, 1)
         ok = __all_sync(0xffffffffu, ok);
         have_o[tile] = ok;
       }
-      if (tile == mt) red[(tile * 2 + mh) * 128 + row] = dsum;
     }
+    // After both tiles' last MMAs (o_full), so nothing reads ring slot 2 now.
+    red[(mt * 2 + mh) * 128 + row] = dsum;
     tc_fence_after();
     // The two column-half partials of every row meet here (fixed order).
     asm volatile("bar.sync 1, %0;" ::"r"(C::kOcticWarps * 32) : "memory");
@@ -711,7 +718,7 @@ __global__ void __launch_bounds__(576, 1)
   uint64_t* o_full = p_full + 2;
   uint64_t* drain = o_full + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
-  uint64_t* q_empty = reinterpret_cast<uint64_t*>(smem + C::RED_OFF);  // the row-sum exchange area is unused here
+  uint64_t* q_empty = reinterpret_cast<uint64_t*>(smem + C::XBAR_OFF);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
