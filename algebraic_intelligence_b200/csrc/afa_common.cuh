@@ -278,6 +278,12 @@ __device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr, uint32_t lbo_byte
   return d;
 }
 
+// The descriptor of the operand `bytes` past the one `d` describes: the start
+// field holds address >> 4 in bits 0-13, so for a 16-byte multiple that keeps
+// the address below 256 KB (every shared-memory address does) the sum moves
+// the start and leaves the other fields as they are.
+__device__ __forceinline__ uint64_t desc_add(uint64_t d, uint32_t bytes) { return d + (bytes >> 4); }
+
 // Instruction descriptor, kind::f16 with bf16 A/B and an fp32 accumulator.
 __host__ __device__ constexpr uint32_t idesc_bf16_f32(int m, int n, bool b_mn_major) {
   return (1u << 4)                                  // D format: F32

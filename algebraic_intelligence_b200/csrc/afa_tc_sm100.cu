@@ -324,23 +324,27 @@ __global__ void __launch_bounds__(576, 1)
     if (lane == 0 && n1 > 0) {
       constexpr uint32_t idesc_s = idesc_bf16_f32(128, 128, false);
       constexpr uint32_t idesc_o = idesc_bf16_f32(128, HD, true);
-      const uint32_t q_base = smem_u32(smem + C::Q_OFF);
-      const uint32_t kv_base = smem_u32(smem + C::KV_OFF);
+      // Base descriptors, built once: the issue loops only add constant
+      // offsets (desc_add), which keeps this thread's instructions between
+      // MMAs few while the octic warps compete for the same issue slots.
+      const uint64_t q_desc = sw128_desc(smem_u32(smem + C::Q_OFF), 16, 1024);
+      const uint64_t k_desc = sw128_desc(smem_u32(smem + C::KV_OFF), 16, 1024);
+      const uint64_t v_desc = sw128_desc(smem_u32(smem + C::KV_OFF), C::SUB_BYTES, 1024);
       auto issue_s = [&](int i, int slot) {
+        const uint64_t kb = desc_add(k_desc, slot * C::TILE_BYTES);
 #pragma unroll
         for (int kk = 0; kk < HD / 16; ++kk) {
-          const uint32_t off = (kk & 3) * 32;
-          const uint64_t a = sw128_desc(q_base + (i * C::KSUB + (kk >> 2)) * C::SUB_BYTES + off, 16, 1024);
-          const uint64_t b = sw128_desc(kv_base + (slot * C::KSUB + (kk >> 2)) * C::SUB_BYTES + off, 16, 1024);
-          umma_ss(tmem + C::s_col(i), a, b, idesc_s, kk > 0 ? 1u : 0u);
+          const uint32_t off = (kk >> 2) * C::SUB_BYTES + (kk & 3) * 32;
+          umma_ss(tmem + C::s_col(i), desc_add(q_desc, i * C::TILE_BYTES + off), desc_add(kb, off), idesc_s,
+                  kk > 0 ? 1u : 0u);
         }
       };
       auto issue_o = [&](int i, int slot, bool acc) {
+        const uint64_t vb = desc_add(v_desc, slot * C::TILE_BYTES);
 #pragma unroll
-        for (int kk = 0; kk < C::BN / 16; ++kk) {
-          const uint64_t b = sw128_desc(kv_base + slot * C::TILE_BYTES + kk * 2048, C::SUB_BYTES, 1024);
-          umma_ts(tmem + C::o_col(i), tmem + C::s_col(i) + C::p_col(kk), b, idesc_o, (acc || kk > 0) ? 1u : 0u);
-        }
+        for (int kk = 0; kk < C::BN / 16; ++kk)
+          umma_ts(tmem + C::o_col(i), tmem + C::s_col(i) + C::p_col(kk), desc_add(vb, kk * 2048), idesc_o,
+                  (acc || kk > 0) ? 1u : 0u);
       };
       bool ok = mbar_wait(q_full, 0, L.status, kDevTimeoutMma) && mbar_wait(kv_full + 0, 0, L.status, kDevTimeoutMma);
       if (ok) {
@@ -793,23 +797,27 @@ __global__ void __launch_bounds__(576, 1)
     if (lane == 0) {
       constexpr uint32_t idesc_s = idesc_bf16_f32(128, 128, false);
       constexpr uint32_t idesc_o = idesc_bf16_f32(128, HD, true);
-      const uint32_t q_base = smem_u32(smem + C::Q_OFF);
-      const uint32_t kv_base = smem_u32(smem + C::KV_OFF);
+      // Base descriptors, built once: the issue loops only add constant
+      // offsets (desc_add), which keeps this thread's instructions between
+      // MMAs few while the octic warps compete for the same issue slots.
+      const uint64_t q_desc = sw128_desc(smem_u32(smem + C::Q_OFF), 16, 1024);
+      const uint64_t k_desc = sw128_desc(smem_u32(smem + C::KV_OFF), 16, 1024);
+      const uint64_t v_desc = sw128_desc(smem_u32(smem + C::KV_OFF), C::SUB_BYTES, 1024);
       auto issue_s = [&](int q, int slot) {
+        const uint64_t kb = desc_add(k_desc, slot * C::TILE_BYTES);
 #pragma unroll
         for (int kk = 0; kk < HD / 16; ++kk) {
-          const uint32_t off = (kk & 3) * 32;
-          const uint64_t a = sw128_desc(q_base + (q * C::KSUB + (kk >> 2)) * C::SUB_BYTES + off, 16, 1024);
-          const uint64_t b = sw128_desc(kv_base + (slot * C::KSUB + (kk >> 2)) * C::SUB_BYTES + off, 16, 1024);
-          umma_ss(tmem + C::s_col(q), a, b, idesc_s, kk > 0 ? 1u : 0u);
+          const uint32_t off = (kk >> 2) * C::SUB_BYTES + (kk & 3) * 32;
+          umma_ss(tmem + C::s_col(q), desc_add(q_desc, q * C::TILE_BYTES + off), desc_add(kb, off), idesc_s,
+                  kk > 0 ? 1u : 0u);
         }
       };
       auto issue_o = [&](int q, int slot, bool acc) {
+        const uint64_t vb = desc_add(v_desc, slot * C::TILE_BYTES);
 #pragma unroll
-        for (int kk = 0; kk < C::BN / 16; ++kk) {
-          const uint64_t b = sw128_desc(kv_base + slot * C::TILE_BYTES + kk * 2048, C::SUB_BYTES, 1024);
-          umma_ts(tmem + C::o_col(q), tmem + C::s_col(q) + C::p_col(kk), b, idesc_o, (acc || kk > 0) ? 1u : 0u);
-        }
+        for (int kk = 0; kk < C::BN / 16; ++kk)
+          umma_ts(tmem + C::o_col(q), tmem + C::s_col(q) + C::p_col(kk), desc_add(vb, kk * 2048), idesc_o,
+                  (acc || kk > 0) ? 1u : 0u);
       };
       SkSeg sg;
       int qn = 0, ub = 0, pc[2] = {0, 0};
