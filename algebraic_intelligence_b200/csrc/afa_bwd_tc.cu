@@ -190,16 +190,18 @@ __device__ __forceinline__ void issue(uint8_t* smem, const Bars& b, uint32_t tme
   if (niter <= 0) return;
   constexpr uint32_t idesc_x = idesc_bf16_f32(128, 128, false);
   constexpr uint32_t idesc_acc = idesc_bf16_f32(128, HD, true);
-  const uint32_t fix = smem_u32(smem + C::FIX_OFF);
-  auto stage = [&](int j) { return smem_u32(smem + C::ST_OFF + (j % C::NST) * 2 * C::TILE_BYTES); };
+  // Base descriptors, built once; the loops add constant offsets (desc_add),
+  // keeping this thread's instructions between MMAs few.
+  const uint64_t fix_k = sw128_desc(smem_u32(smem + C::FIX_OFF), 16, 1024);
+  const uint64_t st_k = sw128_desc(smem_u32(smem + C::ST_OFF), 16, 1024);
+  const uint64_t st_mn = sw128_desc(smem_u32(smem + C::ST_OFF), C::SUB_BYTES, 1024);
+  auto stage = [&](int j) { return static_cast<uint32_t>((j % C::NST) * 2 * C::TILE_BYTES); };
   auto score = [&](int t, int j, uint32_t dst) {  // t = 0: X = F0 S0^T, t = 1: Y = F1 S1^T
-    const uint32_t st = stage(j);
+    const uint64_t sb = desc_add(st_k, stage(j) + t * C::TILE_BYTES);
 #pragma unroll
     for (int kk = 0; kk < HD / 16; ++kk) {
       const uint32_t off = (kk >> 2) * C::SUB_BYTES + (kk & 3) * 32;
-      const uint64_t a = sw128_desc(fix + t * C::TILE_BYTES + off, 16, 1024);
-      const uint64_t bd = sw128_desc(st + t * C::TILE_BYTES + off, 16, 1024);
-      umma_ss(tmem + dst, a, bd, idesc_x, kk > 0 ? 1u : 0u);
+      umma_ss(tmem + dst, desc_add(fix_k, t * C::TILE_BYTES + off), desc_add(sb, off), idesc_x, kk > 0 ? 1u : 0u);
     }
   };
   bool ok = mbar_wait(b.fix_full, 0, status, kDevTimeoutMma) && mbar_wait(b.st_full, 0, status, kDevTimeoutMma);
@@ -225,23 +227,23 @@ __device__ __forceinline__ void issue(uint8_t* smem, const Bars& b, uint32_t tme
     }
     if (!(ok = mbar_wait(b.g_full + (j & 1), (j >> 1) & 1, status, kDevTimeoutMma))) break;
     tc_fence_after();
-    const uint32_t st = stage(j);
+    const uint64_t sm = desc_add(st_mn, stage(j));
     const uint32_t ya = T::y(yb);
     if constexpr (TWO) {
 #pragma unroll
       for (int kk = 0; kk < 8; ++kk) {  // dV += W^T dO
-        const uint64_t m = sw128_desc(st + C::TILE_BYTES + kk * 2048, C::SUB_BYTES, 1024);
+        const uint64_t m = desc_add(sm, C::TILE_BYTES + kk * 2048);
         umma_ts(tmem + T::ACC0, tmem + ya + C::p_col(kk) + 16, m, idesc_acc, (j > 0 || kk > 0) ? 1u : 0u);
       }
 #pragma unroll
       for (int kk = 0; kk < 8; ++kk) {  // dK += dS^T Q
-        const uint64_t m = sw128_desc(st + kk * 2048, C::SUB_BYTES, 1024);
+        const uint64_t m = desc_add(sm, kk * 2048);
         umma_ts(tmem + T::ACC1, tmem + ya + C::p_col(kk), m, idesc_acc, (j > 0 || kk > 0) ? 1u : 0u);
       }
     } else {
 #pragma unroll
       for (int kk = 0; kk < 8; ++kk) {  // dQ += dS K
-        const uint64_t m = sw128_desc(st + kk * 2048, C::SUB_BYTES, 1024);
+        const uint64_t m = desc_add(sm, kk * 2048);
         umma_ts(tmem + T::ACC0, tmem + ya + C::p_col(kk), m, idesc_acc, (j > 0 || kk > 0) ? 1u : 0u);
       }
     }
