@@ -61,12 +61,17 @@ struct TcCfg {
   static constexpr int KV_OFF = 2 * TILE_BYTES;
   static constexpr int BAR_OFF = KV_OFF + NSLOT * TILE_BYTES;
   static constexpr int NBAR = 1 + 2 * NSLOT + 2 + 2 + 2 + 1;
-  static constexpr int XBAR_OFF = BAR_OFF + NBAR * 8;  // one more barrier (the stream-K kernel's q_empty)
+  // Past the common barriers: afa_tc_fwd_kernel keeps its TMEM address at
+  // XBAR_OFF; afa_tc_sk_kernel keeps q_empty there, its TMEM address at +8,
+  // the row-sum exchange barriers of its final-output mode at +16 (2 x 8) and
+  // their fp32 row sums [tile][row] at XRED_OFF.
+  static constexpr int XBAR_OFF = BAR_OFF + NBAR * 8;
+  static constexpr int XRED_OFF = XBAR_OFF + 16 + 16 * 8;
   // fp32 row-sum partials [tile][column half][row] of the epilogue, in K/V
   // ring slot 2 (idle once every MMA has finished; slots 0-1 stage the output
   // tiles).
   static constexpr int RED_OFF = KV_OFF + 2 * TILE_BYTES;
-  static constexpr int SMEM_BYTES = XBAR_OFF + 16 + 1024;
+  static constexpr int SMEM_BYTES = XRED_OFF + 2 * 128 * 4 + 1024;
   static_assert(NSLOT >= 3 && 2 * 2 * 128 * 4 <= TILE_BYTES, "row-sum partials fit in ring slot 2");
   static_assert(SMEM_BYTES <= 227 * 1024, "shared memory per CTA");
   static constexpr uint32_t TMEM_COLS = 512;
@@ -625,11 +630,15 @@ __global__ void __launch_bounds__(576, 1)
 // (sk_finalize_kernel). There is no named barrier and no inter-CTA wait; every
 // wait is a bounded mbarrier wait as in afa_tc_fwd_kernel.
 constexpr int kMaxSkItems = 1024;
+// Final-output launches use the persistent kernel only while their query pairs
+// average at most this many key tiles.
+constexpr int kSkFinalMaxAvgTiles = 12;
 
 struct SkPlan {
   int nitems;                   // listed query pairs per (b, h)
   int nbh;                      // B * H
   int waves;                    // rounds of whole items
+  int snake;                    // 1: whole items only, CTA order reversed every other round (final output)
   int prefix[kMaxSkItems + 1];  // key-tile iterations before listed pair i; prefix[nitems] = per (b, h)
   int pair_of[kMaxSkItems];     // launch pair (pair_geom index) of listed pair i
 };
@@ -659,6 +668,11 @@ struct SkWalk {
     c = c_;
     k = 0;
     total = static_cast<long long>(s.nbh) * s.nitems;
+    if (s.snake) {  // whole items only: no split tail
+      j0 = total;
+      i = hi = 0;
+      return;
+    }
     j0 = static_cast<long long>(s.waves) * G;
     const long long i0 = sk_before(s, j0);
     const long long tail = sk_before(s, total) - i0;
@@ -668,7 +682,11 @@ struct SkWalk {
 
   __device__ __forceinline__ bool next(SkSeg& sg) {
     while (k < S->waves) {  // whole items
-      const long long j = static_cast<long long>(k++) * G + c;
+      // Snake order: in odd rounds CTA c takes the round's (G-1-c)-th item, so
+      // over the rounds of a longest-first list every CTA gets a like share.
+      const int kc = (S->snake && (k & 1)) ? G - 1 - c : c;
+      const long long j = static_cast<long long>(k++) * G + kc;
+      if (j >= total) continue;
       const int item = static_cast<int>(j / S->nbh);
       const int n = S->prefix[item + 1] - S->prefix[item];
       if (n > 0) {
@@ -721,8 +739,11 @@ __global__ void __launch_bounds__(576, 1)
   uint64_t* p_full = s_full + 2;
   uint64_t* o_full = p_full + 2;
   uint64_t* drain = o_full + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   uint64_t* q_empty = reinterpret_cast<uint64_t*>(smem + C::XBAR_OFF);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::XBAR_OFF + 8);
+  uint64_t* xa = reinterpret_cast<uint64_t*>(smem + C::XBAR_OFF + 16);  // [tile * 4 + sub]: half 1's row sums written
+  uint64_t* xb = xa + 8;                                                // [tile * 4 + sub]: row totals written
+  float* xred = reinterpret_cast<float*>(smem + C::XRED_OFF);            // [tile][row]
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -740,6 +761,10 @@ __global__ void __launch_bounds__(576, 1)
       mbar_init(s_full + i, 1);
       mbar_init(p_full + i, 8);  // one elected arrive per octic warp of the tile
       mbar_init(o_full + i, 1);
+    }
+    for (int i = 0; i < 8; ++i) {
+      mbar_init(xa + i, 32);  // every lane of the writing warp arrives
+      mbar_init(xb + i, 32);
     }
     mbar_init(drain, 1);
     fence_barrier_init();
@@ -895,7 +920,7 @@ __global__ void __launch_bounds__(576, 1)
     const uint32_t lane_off = static_cast<uint32_t>(sub * 32) << 16;
     const float scale = L.scale;
     SkSeg sg;
-    int sc = 0, oc = 0;
+    int sc = 0, oc = 0, xc = 0;
     bool ok = true;
     while (ok && walk.next(sg)) {
       const PairGeom G = pair_geom(L, S.pair_of[sg.item]);
@@ -931,9 +956,78 @@ __global__ void __launch_bounds__(576, 1)
         __syncwarp();
         if (lane == 0) mbar_arrive(p_full + mt);
       }
-      // Add this piece into the accumulators: this warp's O columns of its
-      // tile and its partial row sum (two adds per row).
-      if (ok && sg.t0 < tend) {
+      if (L.mode == kFinal) {
+        // Final output of a whole item (snake plans): out = O / (d + sink) in
+        // bf16 and d_total = d + sink, d being the two column halves' row sums
+        // added in a fixed order, half 0 first, as afa_tc_fwd_kernel adds them.
+        // Half 1 posts its sums, half 0 forms the totals and posts them back.
+        const bool live = sg.t0 < tend;
+        const int xi = mt * 4 + sub;
+        float total = 0.f;
+        if (ok && live) {
+          float* const xr = xred + mt * 128 + row;
+          if (mh == 1) {
+            *xr = dsum;
+            mbar_arrive(xa + xi);
+            ok = mbar_wait(xb + xi, xc & 1, L.status, kDevTimeoutEpilogue);
+            total = *xr;
+          } else {
+            ok = mbar_wait(xa + xi, xc & 1, L.status, kDevTimeoutEpilogue);
+            total = dsum + *xr;
+            *xr = total;
+            mbar_arrive(xb + xi);
+          }
+          ++xc;
+          ok = __all_sync(0xffffffffu, ok);
+          if (ok) {
+            ok = mbar_wait(o_full + mt, oc & 1, L.status, kDevTimeoutEpilogue);
+            ++oc;
+            ok = __all_sync(0xffffffffu, ok);
+          }
+        }
+        if (ok) {
+          tc_fence_after();
+          const float denom = total + L.sink;
+          const float inv = 1.0f / denom;
+          // Each lane packs 32 columns of its row into four 16-byte chunks;
+          // transposed in groups of 4 lanes, a store instruction then writes 64
+          // contiguous bytes of each of 8 rows.
+          constexpr int NCH = 4;
+          const int gi = lane % NCH;
+          const int grow0 = G.r0 + 128 * mt + sub * 32 + (lane / NCH) * NCH;  // the group's first row
+          const long long gbase = static_cast<long long>(sg.bh) * L.lq + P.q.row0;
+#pragma unroll 1
+          for (int c = 0; c < HD / 64; ++c) {
+            const int col0 = (HD / 2) * mh + 32 * c;
+            uint32_t ov[32];
+            if (live) {
+              __syncwarp();  // tcgen05.ld is warp-collective
+              tmem_ld32(tmem + C::o_col(mt) + lane_off + col0, ov);
+              tmem_ld_wait();
+            } else {
+#pragma unroll
+              for (int e = 0; e < 32; ++e) ov[e] = 0u;
+            }
+            uint32_t pk[32];
+#pragma unroll
+            for (int w = 0; w < 16; ++w)
+              pk[w] = pack_bf16x2(__uint_as_float(ov[2 * w]) * inv, __uint_as_float(ov[2 * w + 1]) * inv);
+            transpose_chunks<NCH>(pk, gi);
+#pragma unroll
+            for (int kr = 0; kr < NCH; ++kr) {
+              if (grow0 + kr < P.q.len)
+                *reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(L.out) + (gbase + grow0 + kr) * HD + col0 +
+                                          8 * gi) = make_uint4(pk[4 * kr], pk[4 * kr + 1], pk[4 * kr + 2],
+                                                               pk[4 * kr + 3]);
+            }
+          }
+          const int rloc = G.r0 + 128 * mt + row;
+          if (mh == 0 && L.dtot && rloc < P.q.len)
+            static_cast<float*>(L.dtot)[static_cast<long long>(sg.bh) * L.lq + P.q.row0 + rloc] = denom;
+        }
+      } else if (ok && sg.t0 < tend) {
+        // Add this piece into the accumulators: this warp's O columns of its
+        // tile and its partial row sum (two adds per row).
         ok = mbar_wait(o_full + mt, oc & 1, L.status, kDevTimeoutEpilogue);
         ++oc;
         ok = __all_sync(0xffffffffu, ok);
@@ -1049,12 +1143,9 @@ cudaError_t launch_hd(const Launch& L, cudaStream_t stream, const char** detail)
   Launch LL = L;
   const int total = assign_ctas(LL, 256);
   if (total == 0) return cudaSuccess;
-  if ((LL.mode == kAccumRaw || LL.mode == kAccumFinal) && total <= kMaxSkItems && dev < 64) {
-    // Accumulate modes: persistent stream-K over equal shares of the key-tile
-    // iterations, pieces added with reductions; then the divide for kAccumFinal.
-    // The pairs with key tiles, longest first (stable): whole-item rounds then
-    // hold items of similar length.
-    SkPlan S;
+  // The pairs with key tiles, longest first (stable): whole-item rounds then
+  // hold items of similar length.
+  auto make_plan = [&](SkPlan& S) {
     int len[kMaxSkItems];
     S.nitems = 0;
     for (int c = 0; c < total; ++c) {
@@ -1065,6 +1156,34 @@ cudaError_t launch_hd(const Launch& L, cudaStream_t stream, const char** detail)
     S.nbh = bh;
     S.prefix[0] = 0;
     for (int i = 0; i < S.nitems; ++i) S.prefix[i + 1] = S.prefix[i] + len[S.pair_of[i]];
+    S.snake = 0;
+  };
+  if (LL.mode == kFinal && LL.out && total <= kMaxSkItems && dev < 64 &&
+      static_cast<long long>(bh) * total > sm_count[dev]) {
+    // More query pairs than SMs, and short ones: one persistent CTA per SM
+    // walks whole pairs, longest first in snake order, so a CTA's next pair
+    // starts (Q load, first scores) while its previous pair's last P.V and
+    // output run. Measured on B200: +5.6% at L=2048 causal (9 key tiles per
+    // pair on average), even at L=4096 (17), 3-6% slower at L=65536, so pairs
+    // of more than kSkFinalMaxAvgTiles key tiles on average keep one CTA per
+    // pair. Every pair must have key tiles: a pair the plan leaves out would
+    // leave its output rows unwritten.
+    SkPlan S;
+    make_plan(S);
+    if (S.nitems == total && S.prefix[S.nitems] <= kSkFinalMaxAvgTiles * S.nitems) {
+      S.snake = 1;
+      const long long items = static_cast<long long>(bh) * S.nitems;
+      const int G = static_cast<int>(items < sm_count[dev] ? items : sm_count[dev]);
+      S.waves = static_cast<int>((items + G - 1) / G);
+      afa_tc_sk_kernel<HD><<<G, C::kThreads, C::SMEM_BYTES, stream>>>(tq, tk, tv, LL, S);
+      return cudaGetLastError();
+    }
+  }
+  if ((LL.mode == kAccumRaw || LL.mode == kAccumFinal) && total <= kMaxSkItems && dev < 64) {
+    // Accumulate modes: persistent stream-K over equal shares of the key-tile
+    // iterations, pieces added with reductions; then the divide for kAccumFinal.
+    SkPlan S;
+    make_plan(S);
     const long long W = static_cast<long long>(bh) * S.prefix[S.nitems];
     if (W > 0) {
       long long G = W / 8;  // at least 8 key tiles per CTA
