@@ -314,3 +314,86 @@ def test_host_chunks_cover_every_head_once(bh, per):
     edge = max(1, per // 2)
     if bh > edge:
         assert ch[0][1] - ch[0][0] == edge
+
+
+# ---------------------------------------------------------------------------
+# The persistent kernel's work walk (afa_tc_sk_kernel, SkWalk in
+# csrc/afa_tc_sm100.cu), restated: whole-item rounds, then an even split of the
+# remaining key-tile iterations (accumulate hops), or whole items only in snake
+# order (final output of short-pair prefills).
+# ---------------------------------------------------------------------------
+def _sk_before(prefix, nitems, nbh, j):
+    pair, hh = divmod(j, nbh)
+    base = nbh * prefix[pair]
+    return base if pair >= nitems else base + hh * (prefix[pair + 1] - prefix[pair])
+
+
+def _sk_walk(prefix, nitems, nbh, waves, snake, G, c):
+    """The (bh, item, t0, t1) pieces CTA c of G computes, in order."""
+    total = nbh * nitems
+    out = []
+    for k in range(waves):
+        kc = G - 1 - c if (snake and k & 1) else c
+        j = k * G + kc
+        if j >= total:
+            continue
+        item, bh = divmod(j, nbh)
+        n = prefix[item + 1] - prefix[item]
+        if n > 0:
+            out.append((bh, item, 0, n))
+    if snake:
+        return out
+    j0 = waves * G
+    i0 = _sk_before(prefix, nitems, nbh, j0)
+    tail = _sk_before(prefix, nitems, nbh, total) - i0
+    i, hi = i0 + tail * c // G, i0 + tail * (c + 1) // G
+    while i < hi:
+        lo, up = j0, total
+        while up - lo > 1:
+            mid = (lo + up) >> 1
+            if _sk_before(prefix, nitems, nbh, mid) <= i:
+                lo = mid
+            else:
+                up = mid
+        item, bh = divmod(lo, nbh)
+        t0 = i - _sk_before(prefix, nitems, nbh, lo)
+        n = prefix[item + 1] - prefix[item]
+        t1 = min(t0 + (hi - i), n)
+        out.append((bh, item, t0, t1))
+        i += t1 - t0
+    return out
+
+
+@pytest.mark.parametrize("snake", [False, True])
+@pytest.mark.parametrize("seed", range(6))
+def test_sk_walk_covers_every_key_tile_once(seed, snake):
+    rng = np.random.default_rng(seed)
+    nitems = int(rng.integers(1, 40))
+    nbh = int(rng.integers(1, 70))
+    lens = sorted((int(x) for x in rng.integers(1, 60, size=nitems)), reverse=True)
+    prefix = np.concatenate([[0], np.cumsum(lens)]).tolist()
+    items = nbh * nitems
+    G = int(min(148, items if snake else max(1, nbh * prefix[-1] // 8)))
+    waves = -(-items // G) if snake else items // G
+    seen = {}
+    for c in range(G):
+        for bh, item, t0, t1 in _sk_walk(prefix, nitems, nbh, waves, snake, G, c):
+            assert 0 <= t0 < t1 <= lens[item]
+            if snake:
+                assert (t0, t1) == (0, lens[item]), "final-output pieces are whole items"
+            for t in range(t0, t1):
+                assert (bh, item, t) not in seen
+                seen[(bh, item, t)] = c
+    assert len(seen) == nbh * prefix[-1]
+
+
+def test_sk_walk_snake_balances_longest_first_lists():
+    """Snake order over a longest-first list: every CTA's share of key tiles is
+    within one item of the mean (config 3's causal pairs on 148 CTAs)."""
+    nbh, npair = 64, 16
+    lens = [2 * p + 2 for p in reversed(range(npair))]
+    prefix = np.concatenate([[0], np.cumsum(lens)]).tolist()
+    G = 148
+    waves = -(-nbh * npair // G)
+    work = [sum(t1 - t0 for _, _, t0, t1 in _sk_walk(prefix, npair, nbh, waves, True, G, c)) for c in range(G)]
+    assert max(work) - min(work) <= max(lens)
