@@ -632,13 +632,12 @@ __global__ void __launch_bounds__(576, 1)
 constexpr int kMaxSkItems = 1024;
 // Final-output launches use the persistent kernel only while their query pairs
 // average at most this many key tiles.
-constexpr int kSkFinalMaxAvgTiles = 12;
+constexpr int kSkFinalMaxAvgTiles = 32;
 
 struct SkPlan {
   int nitems;                   // listed query pairs per (b, h)
   int nbh;                      // B * H
   int waves;                    // rounds of whole items
-  int snake;                    // 1: whole items only, CTA order reversed every other round (final output)
   int prefix[kMaxSkItems + 1];  // key-tile iterations before listed pair i; prefix[nitems] = per (b, h)
   int pair_of[kMaxSkItems];     // launch pair (pair_geom index) of listed pair i
 };
@@ -656,8 +655,47 @@ __host__ __device__ __forceinline__ long long sk_before(const SkPlan& S, long lo
 }
 
 // The pieces CTA c of G computes, in order; every role of the CTA walks the
-// same sequence.
-struct SkWalk {
+// same sequence. SNAKE (the final-output mode): whole items only, and in odd
+// rounds CTA c takes the round's (G-1-c)-th item, so over the rounds of a
+// longest-first list every CTA gets a like share. Otherwise whole-item rounds
+// are followed by the even split of the remaining iterations.
+template <bool SNAKE>
+struct SkWalk;
+
+template <>
+struct SkWalk<true> {
+  const SkPlan* S;
+  int G, c, k, total;
+
+  __device__ __forceinline__ void init(const SkPlan& s, int G_, int c_) {
+    S = &s;
+    G = G_;
+    c = c_;
+    k = 0;
+    total = s.nbh * s.nitems;
+  }
+
+  __device__ __forceinline__ bool next(SkSeg& sg) {
+    while (k < S->waves) {
+      const int j = k * G + ((k & 1) ? G - 1 - c : c);
+      ++k;
+      if (j >= total) continue;
+      const int item = j / S->nbh;
+      const int n = S->prefix[item + 1] - S->prefix[item];
+      if (n > 0) {
+        sg.bh = j - item * S->nbh;
+        sg.item = item;
+        sg.t0 = 0;
+        sg.t1 = n;
+        return true;
+      }
+    }
+    return false;
+  }
+};
+
+template <>
+struct SkWalk<false> {
   const SkPlan* S;
   int G, c, k;
   long long j0, total, i, hi;
@@ -668,11 +706,6 @@ struct SkWalk {
     c = c_;
     k = 0;
     total = static_cast<long long>(s.nbh) * s.nitems;
-    if (s.snake) {  // whole items only: no split tail
-      j0 = total;
-      i = hi = 0;
-      return;
-    }
     j0 = static_cast<long long>(s.waves) * G;
     const long long i0 = sk_before(s, j0);
     const long long tail = sk_before(s, total) - i0;
@@ -682,11 +715,7 @@ struct SkWalk {
 
   __device__ __forceinline__ bool next(SkSeg& sg) {
     while (k < S->waves) {  // whole items
-      // Snake order: in odd rounds CTA c takes the round's (G-1-c)-th item, so
-      // over the rounds of a longest-first list every CTA gets a like share.
-      const int kc = (S->snake && (k & 1)) ? G - 1 - c : c;
-      const long long j = static_cast<long long>(k++) * G + kc;
-      if (j >= total) continue;
+      const long long j = static_cast<long long>(k++) * G + c;
       const int item = static_cast<int>(j / S->nbh);
       const int n = S->prefix[item + 1] - S->prefix[item];
       if (n > 0) {
@@ -723,7 +752,9 @@ __device__ __forceinline__ void red_add(float* p, float a) {
   asm volatile("red.global.add.f32 [%0], %1;" ::"l"(p), "f"(a) : "memory");
 }
 
-template <int HD>
+// FINAL: the final-output mode (kFinal launches, snake plans, bf16 output and
+// d_total written per pair); otherwise the accumulate hop modes.
+template <int HD, bool FINAL>
 __global__ void __launch_bounds__(576, 1)
     afa_tc_sk_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                      const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ Launch L,
@@ -747,7 +778,7 @@ __global__ void __launch_bounds__(576, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  SkWalk walk;
+  SkWalk<FINAL> walk;
   walk.init(S, gridDim.x, blockIdx.x);
 
   if (threadIdx.x == 0) {
@@ -956,7 +987,7 @@ __global__ void __launch_bounds__(576, 1)
         __syncwarp();
         if (lane == 0) mbar_arrive(p_full + mt);
       }
-      if (L.mode == kFinal) {
+      if constexpr (FINAL) {
         // Final output of a whole item (snake plans): out = O / (d + sink) in
         // bf16 and d_total = d + sink, d being the two column halves' row sums
         // added in a fixed order, half 0 first, as afa_tc_fwd_kernel adds them.
@@ -1025,7 +1056,7 @@ __global__ void __launch_bounds__(576, 1)
           if (mh == 0 && L.dtot && rloc < P.q.len)
             static_cast<float*>(L.dtot)[static_cast<long long>(sg.bh) * L.lq + P.q.row0 + rloc] = denom;
         }
-      } else if (ok && sg.t0 < tend) {
+      } else if (ok && sg.t0 < tend) {  // accumulate modes
         // Add this piece into the accumulators: this warp's O columns of its
         // tile and its partial row sum (two adds per row).
         ok = mbar_wait(o_full + mt, oc & 1, L.status, kDevTimeoutEpilogue);
@@ -1125,7 +1156,11 @@ cudaError_t launch_hd(const Launch& L, cudaStream_t stream, const char** detail)
     cudaError_t e = cudaFuncSetAttribute(afa_tc_fwd_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          C::SMEM_BYTES);
     if (e == cudaSuccess)
-      e = cudaFuncSetAttribute(afa_tc_sk_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
+      e = cudaFuncSetAttribute(afa_tc_sk_kernel<HD, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               C::SMEM_BYTES);
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(afa_tc_sk_kernel<HD, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               C::SMEM_BYTES);
     if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sm_count[dev], cudaDevAttrMultiProcessorCount, dev);
     if (e != cudaSuccess) {
       *detail = "cudaFuncSetAttribute(max dynamic shared memory) failed";
@@ -1156,26 +1191,25 @@ cudaError_t launch_hd(const Launch& L, cudaStream_t stream, const char** detail)
     S.nbh = bh;
     S.prefix[0] = 0;
     for (int i = 0; i < S.nitems; ++i) S.prefix[i + 1] = S.prefix[i] + len[S.pair_of[i]];
-    S.snake = 0;
   };
   if (LL.mode == kFinal && LL.out && total <= kMaxSkItems && dev < 64 &&
       static_cast<long long>(bh) * total > sm_count[dev]) {
-    // More query pairs than SMs, and short ones: one persistent CTA per SM
+    // More query pairs than SMs, and not long ones: one persistent CTA per SM
     // walks whole pairs, longest first in snake order, so a CTA's next pair
     // starts (Q load, first scores) while its previous pair's last P.V and
-    // output run. Measured on B200: +5.6% at L=2048 causal (9 key tiles per
-    // pair on average), even at L=4096 (17), 3-6% slower at L=65536, so pairs
-    // of more than kSkFinalMaxAvgTiles key tiles on average keep one CTA per
-    // pair. Every pair must have key tiles: a pair the plan leaves out would
-    // leave its output rows unwritten.
+    // output run. Measured on B200: +5% at L=2048 causal (9 key tiles per
+    // pair on average), +3.7% at L=4096 (17), even at L=65536 (257), where
+    // per-CTA set-up is already negligible; pairs of more than
+    // kSkFinalMaxAvgTiles key tiles on average keep one CTA per pair. Every
+    // pair must have key tiles: a pair the plan leaves out would leave its
+    // output rows unwritten.
     SkPlan S;
     make_plan(S);
     if (S.nitems == total && S.prefix[S.nitems] <= kSkFinalMaxAvgTiles * S.nitems) {
-      S.snake = 1;
       const long long items = static_cast<long long>(bh) * S.nitems;
       const int G = static_cast<int>(items < sm_count[dev] ? items : sm_count[dev]);
       S.waves = static_cast<int>((items + G - 1) / G);
-      afa_tc_sk_kernel<HD><<<G, C::kThreads, C::SMEM_BYTES, stream>>>(tq, tk, tv, LL, S);
+      afa_tc_sk_kernel<HD, true><<<G, C::kThreads, C::SMEM_BYTES, stream>>>(tq, tk, tv, LL, S);
       return cudaGetLastError();
     }
   }
@@ -1190,7 +1224,8 @@ cudaError_t launch_hd(const Launch& L, cudaStream_t stream, const char** detail)
       if (G > sm_count[dev]) G = sm_count[dev];
       if (G < 1) G = 1;
       S.waves = static_cast<int>(static_cast<long long>(bh) * S.nitems / G);
-      afa_tc_sk_kernel<HD><<<static_cast<int>(G), C::kThreads, C::SMEM_BYTES, stream>>>(tq, tk, tv, LL, S);
+      afa_tc_sk_kernel<HD, false><<<static_cast<int>(G), C::kThreads, C::SMEM_BYTES, stream>>>(tq, tk, tv, LL,
+                                                                                               S);
       cudaError_t e = cudaGetLastError();
       if (e != cudaSuccess) return e;
     }
