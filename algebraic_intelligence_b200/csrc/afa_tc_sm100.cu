@@ -629,6 +629,13 @@ __global__ void __launch_bounds__(576, 1)
 // In kAccumFinal the divide runs afterwards over the problems' rows
 // (sk_finalize_kernel). There is no named barrier and no inter-CTA wait; every
 // wait is a bounded mbarrier wait as in afa_tc_fwd_kernel.
+//
+// Final-output mode (FINAL = true, kFinal prefills of many short pairs): the
+// same CTAs walk whole pairs only, in snake order over a longest-first list,
+// and each pair's octic warps write its bf16 output and d_total themselves,
+// so a CTA's next pair loads and computes its first scores while the previous
+// pair's last P.V and output run. There is no per-pair CTA launch, set-up or
+// teardown.
 constexpr int kMaxSkItems = 1024;
 // Final-output launches use the persistent kernel only while their query pairs
 // average at most this many key tiles.
