@@ -534,20 +534,21 @@ template <int HD>
 cudaError_t launch_bwd_tc_hd(const void* q, const void* k, const void* v, const void* g, const BwdTcArgs& A, int bh,
                              cudaStream_t stream, const char** detail) {
   using C = BwdCfg<HD>;
-  static bool attr_set[64] = {};
+  static PerDeviceOnce setup;
   int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev < 64 && !attr_set[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(afa_bwd_dkv_tc_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         C::SMEM_BYTES);
-    if (e == cudaSuccess)
-      e = cudaFuncSetAttribute(afa_bwd_dq_tc_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               C::SMEM_BYTES);
-    if (e != cudaSuccess) {
-      *detail = "cudaFuncSetAttribute(max dynamic shared memory) failed";
+  cudaError_t se = cudaGetDevice(&dev);
+  if (se == cudaSuccess)
+    se = setup.run(dev, [&] {
+      cudaError_t e = cudaFuncSetAttribute(afa_bwd_dkv_tc_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           C::SMEM_BYTES);
+      if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(afa_bwd_dq_tc_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 C::SMEM_BYTES);
       return e;
-    }
-    attr_set[dev] = true;
+    });
+  if (se != cudaSuccess) {
+    *detail = "cudaFuncSetAttribute(max dynamic shared memory) failed";
+    return se;
   }
   CUtensorMap tq, tg, tk, tv;
   if (!make_tmap(&tq, q, HD, A.L, bh) || !make_tmap(&tg, g, HD, A.L, bh) || !make_tmap(&tk, k, HD, A.L, bh) ||

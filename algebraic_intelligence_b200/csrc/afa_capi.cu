@@ -43,15 +43,17 @@ int cuda_fail(cudaError_t e, const char* what, const char* detail = nullptr) {
 }
 
 int* status_ptr() {
-  static int* ptrs[64] = {};
+  static afa::PerDeviceOnce setup;
+  static int* ptrs[afa::kMaxDevices] = {};
   int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
-  if (!ptrs[dev]) {
+  if (cudaGetDevice(&dev) != cudaSuccess) return nullptr;
+  const cudaError_t e = setup.run(dev, [&] {
     void* p = nullptr;
-    if (cudaGetSymbolAddress(&p, g_afa_device_status) != cudaSuccess) return nullptr;
+    const cudaError_t r = cudaGetSymbolAddress(&p, g_afa_device_status);
     ptrs[dev] = static_cast<int*>(p);
-  }
-  return ptrs[dev];
+    return r;
+  });
+  return e == cudaSuccess ? ptrs[dev] : nullptr;
 }
 
 bool finite_nonneg(double x) { return std::isfinite(x) && x >= 0.0; }

@@ -6,9 +6,31 @@
 #include <cstdint>
 #include <cuda_runtime.h>
 
+#include <mutex>
+
 #include "afa_problem.h"
 
 namespace afa {
+
+constexpr int kMaxDevices = 64;
+
+// Host set-up that runs once per device (kernel attributes, device
+// properties), safe when several host threads make their first call on one
+// device at the same time. The set-up's status is kept and returned to every
+// caller; a device index outside [0, kMaxDevices) is an error.
+class PerDeviceOnce {
+ public:
+  template <class F>
+  cudaError_t run(int dev, F&& init) {
+    if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
+    std::call_once(once_[dev], [&] { status_[dev] = init(); });
+    return status_[dev];
+  }
+
+ private:
+  std::once_flag once_[kMaxDevices];
+  cudaError_t status_[kMaxDevices] = {};
+};
 
 enum Dtype : int { kF32 = 0, kBF16 = 1, kF16 = 2, kF64 = 3 };
 

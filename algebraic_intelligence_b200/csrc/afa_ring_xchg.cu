@@ -25,17 +25,15 @@ static_assert(sizeof(cudaIpcMemHandle_t) == AFA_RING_HANDLE_BYTES, "IPC handle s
 
 namespace {
 
+// Resolved once (a function-local static is initialised once, thread-safely).
 PFN_cuMemGetAddressRange_v3020 address_range_fn() {
-  static PFN_cuMemGetAddressRange_v3020 fn = nullptr;
-  static bool tried = false;
-  if (!tried) {
-    tried = true;
+  static const PFN_cuMemGetAddressRange_v3020 fn = [] {
     void* p = nullptr;
     cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuMemGetAddressRange", &p, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<PFN_cuMemGetAddressRange_v3020>(p);
-  }
+    const bool ok = cudaGetDriverEntryPoint("cuMemGetAddressRange", &p, cudaEnableDefault, &q) == cudaSuccess &&
+                    q == cudaDriverEntryPointSuccess;
+    return ok ? reinterpret_cast<PFN_cuMemGetAddressRange_v3020>(p) : nullptr;
+  }();
   return fn;
 }
 

@@ -1155,25 +1155,26 @@ __global__ void __launch_bounds__(256) sk_finalize_kernel(const __grid_constant_
 template <int HD>
 cudaError_t launch_hd(const Launch& L, cudaStream_t stream, const char** detail) {
   using C = TcCfg<HD>;
-  static bool attr_set[64] = {};
+  static PerDeviceOnce setup;
+  static int sm_count[kMaxDevices] = {};
   int dev = 0;
-  cudaGetDevice(&dev);
-  static int sm_count[64] = {};
-  if (dev < 64 && !attr_set[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(afa_tc_fwd_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         C::SMEM_BYTES);
-    if (e == cudaSuccess)
-      e = cudaFuncSetAttribute(afa_tc_sk_kernel<HD, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               C::SMEM_BYTES);
-    if (e == cudaSuccess)
-      e = cudaFuncSetAttribute(afa_tc_sk_kernel<HD, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               C::SMEM_BYTES);
-    if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sm_count[dev], cudaDevAttrMultiProcessorCount, dev);
-    if (e != cudaSuccess) {
-      *detail = "cudaFuncSetAttribute(max dynamic shared memory) failed";
+  cudaError_t se = cudaGetDevice(&dev);
+  if (se == cudaSuccess)
+    se = setup.run(dev, [&] {
+      cudaError_t e = cudaFuncSetAttribute(afa_tc_fwd_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           C::SMEM_BYTES);
+      if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(afa_tc_sk_kernel<HD, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 C::SMEM_BYTES);
+      if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(afa_tc_sk_kernel<HD, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 C::SMEM_BYTES);
+      if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sm_count[dev], cudaDevAttrMultiProcessorCount, dev);
       return e;
-    }
-    attr_set[dev] = true;
+    });
+  if (se != cudaSuccess) {
+    *detail = "kernel set-up failed (max dynamic shared memory attribute or SM count)";
+    return se;
   }
   CUtensorMap tq, tk, tv, to;
   const int bh = L.B * L.H;
@@ -1199,8 +1200,7 @@ cudaError_t launch_hd(const Launch& L, cudaStream_t stream, const char** detail)
     S.prefix[0] = 0;
     for (int i = 0; i < S.nitems; ++i) S.prefix[i + 1] = S.prefix[i] + len[S.pair_of[i]];
   };
-  if (LL.mode == kFinal && LL.out && total <= kMaxSkItems && dev < 64 &&
-      static_cast<long long>(bh) * total > sm_count[dev]) {
+  if (LL.mode == kFinal && LL.out && total <= kMaxSkItems && static_cast<long long>(bh) * total > sm_count[dev]) {
     // More query pairs than SMs, and not long ones: one persistent CTA per SM
     // walks whole pairs, longest first in snake order, so a CTA's next pair
     // starts (Q load, first scores) while its previous pair's last P.V and
@@ -1220,7 +1220,7 @@ cudaError_t launch_hd(const Launch& L, cudaStream_t stream, const char** detail)
       return cudaGetLastError();
     }
   }
-  if ((LL.mode == kAccumRaw || LL.mode == kAccumFinal) && total <= kMaxSkItems && dev < 64) {
+  if ((LL.mode == kAccumRaw || LL.mode == kAccumFinal) && total <= kMaxSkItems) {
     // Accumulate modes: persistent stream-K over equal shares of the key-tile
     // iterations, pieces added with reductions; then the divide for kAccumFinal.
     SkPlan S;
