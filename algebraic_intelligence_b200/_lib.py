@@ -28,7 +28,8 @@ SIGNATURES = {
     "afa_fwd_hop": (_c_int, [_c_void_p] * 7 + [_c_int] * 6 + [_c_void_p, _c_int, _c_int, _c_int, _c_float,
                                                               _c_void_p]),
     "afa_finalize": (_c_int, [_c_void_p] * 4 + [_c_ll, _c_int, _c_int, _c_float, _c_void_p]),
-    "afa_bwd": (_c_int, [_c_void_p] * 9 + [_c_int] * 7 + [_c_void_p, _c_size, _c_void_p]),
+    "afa_bwd": (_c_int, [_c_void_p] * 9 + [_c_int] * 5 + [_c_float, _c_int, _c_int, _c_void_p, _c_size,
+                                                           _c_void_p]),
     "afa_bwd_workspace_bytes": (_c_size, [_c_int] * 5),
     "afa_ago_table": (_c_int, [_c_void_p, _c_void_p, _c_int, _c_int, ctypes.POINTER(_c_double), _c_double, _c_int,
                                _c_void_p]),

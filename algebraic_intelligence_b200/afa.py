@@ -221,7 +221,7 @@ def tiled_afa_forward(q, k, v, sink_omega: float = 0.5, causal: bool = False, bl
     return _launch_fwd(q, k, v, sink_omega, causal, valid_seq_len, return_denominator)
 
 
-def _launch_bwd(q, k, v, out, d_total, g_out, causal, valid_seq_len):
+def _launch_bwd(q, k, v, out, d_total, g_out, sink_omega, causal, valid_seq_len):
     """dq, dk, dv through afa_bwd; all arguments are contiguous CUDA tensors."""
     b, h, l, d = q.shape
     code = _lib.dtype_code(q.dtype)
@@ -232,7 +232,8 @@ def _launch_bwd(q, k, v, out, d_total, g_out, causal, valid_seq_len):
     dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
     with torch.cuda.device(q.device):
         rc = lib.afa_bwd(q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), den.data_ptr(), g_out.data_ptr(),
-                         dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), b, h, l, d, code, int(bool(causal)),
+                         dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), b, h, l, d, code, float(sink_omega),
+                         int(bool(causal)),
                          int(valid_seq_len or 0), ws.data_ptr(), need, _lib.stream_ptr(q.device))
     _lib.check(rc, "afa_bwd")
     return dq, dk, dv
@@ -244,12 +245,15 @@ def tiled_afa_backward(q, k, v, out, d_total, g_out, sink_omega: float = 0.5, ca
 
     Returns (dq, dk, dv) in q's dtype: the gradients of sum(out * g_out) for
     out = AFA(q, k, v), given the forward's ``out`` and ``d_total`` (row sum +
-    sink, from ``return_denominator=True``). As in the reference the sink
-    enters only through ``d_total`` (:429), and bfloat16 inputs round the
-    weights and score gradients to bfloat16 before the three products with fp32
-    accumulation (:440-448). ``block_q`` / ``block_k`` do not change the result.
+    sink, from ``return_denominator=True``). As in the reference the gradient
+    math uses the sink only through ``d_total`` (:429); ``d_total - sink_omega``
+    (a row's weight sum) tells the kernels which rows lie wholly in the negative
+    tail of the weight map. bfloat16 inputs round the weights and score
+    gradients to bfloat16 before the three products with fp32 accumulation
+    (:440-448). ``block_q`` / ``block_k`` do not change the result.
     """
-    del sink_omega
+    if not _sink_ok(sink_omega):
+        raise ValueError("sink_omega must be finite and nonnegative")
     arrays = (q, k, v, out, g_out)
     if any(a.ndim != 4 for a in arrays) or any(tuple(a.shape) != tuple(q.shape) for a in arrays):
         raise ValueError("q, k, v, out and g_out must have the same four-dimensional shape")
@@ -265,7 +269,7 @@ def tiled_afa_backward(q, k, v, out, d_total, g_out, sink_omega: float = 0.5, ca
     q, k, v, out, d_total, g_out = st.tensors
     if len({t.dtype for t in (q, k, v, out, g_out)}) != 1:
         raise TypeError("q, k, v, out and g_out must share a dtype")
-    return tuple(st.back(t) for t in _launch_bwd(q, k, v, out, d_total, g_out, causal, valid_seq_len))
+    return tuple(st.back(t) for t in _launch_bwd(q, k, v, out, d_total, g_out, sink_omega, causal, valid_seq_len))
 
 
 class _PallasAfa(torch.autograd.Function):
@@ -275,13 +279,13 @@ class _PallasAfa(torch.autograd.Function):
     def forward(ctx, q, k, v, sink_omega, causal, valid_seq_len):
         out, den = _launch_fwd(q, k, v, sink_omega, causal, valid_seq_len, True)
         ctx.save_for_backward(q, k, v, out, den)
-        ctx.causal, ctx.valid_seq_len = causal, valid_seq_len
+        ctx.sink, ctx.causal, ctx.valid_seq_len = sink_omega, causal, valid_seq_len
         return out
 
     @staticmethod
     def backward(ctx, g_out):
         q, k, v, out, den = ctx.saved_tensors
-        dq, dk, dv = _launch_bwd(q, k, v, out, den, g_out.contiguous(), ctx.causal, ctx.valid_seq_len)
+        dq, dk, dv = _launch_bwd(q, k, v, out, den, g_out.contiguous(), ctx.sink, ctx.causal, ctx.valid_seq_len)
         return dq, dk, dv, None, None, None
 
 
@@ -329,7 +333,9 @@ def afa_decode(q, k_cache, v_cache, sink_omega: float = 0.5, kv_len=None, return
     """One decode step: exact AFA for a single query token over a KV cache.
 
     q: (B, H, D) or (B, H, 1, D); k_cache, v_cache: (B, H, Lkv, D). ``kv_len``
-    is an int (visible prefix for every batch row) or a per-batch int tensor.
+    is an int (visible prefix for every batch row) or a per-batch int tensor
+    (host entries must lie in [0, Lkv]; device entries are clamped to it). A
+    row of length 0 gives output 0 and d_total = sink_omega.
     Math = ``pallas_afa_forward`` with one query row, non-causal; oracle =
     reference_afa with Lq = 1 (tests/reference_attention.py:44-59).
     """
@@ -351,6 +357,8 @@ def afa_decode(q, k_cache, v_cache, sink_omega: float = 0.5, kv_len=None, return
             scalar_len = kv_len
         else:
             lens_t = torch.as_tensor(kv_len, dtype=torch.int32)
+            if not lens_t.is_cuda and bool(((lens_t < 0) | (lens_t > lkv)).any()):
+                raise ValueError("kv_len entries must be in [0, cache length]")
     st = Staged(q, k_cache, v_cache)
     qt, kt, vt = st.tensors
     if lens_t is not None:

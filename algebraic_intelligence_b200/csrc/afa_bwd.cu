@@ -399,7 +399,8 @@ extern "C" size_t afa_bwd_workspace_bytes(int B, int H, int L, int D, int dtype)
 
 extern "C" int afa_bwd(const void* q, const void* k, const void* v, const void* out, const void* d_total,
                        const void* g_out, void* dq, void* dk, void* dv, int B, int H, int L, int D, int dtype,
-                       int causal, int valid_len, void* workspace, size_t workspace_bytes, void* stream) {
+                       float sink_omega, int causal, int valid_len, void* workspace, size_t workspace_bytes,
+                       void* stream) {
   using namespace afa;
   if (dtype == AFA_F16)
     return set_last_error(AFA_ERR_DTYPE, "float16 is not supported (the forward rejects it); use bfloat16 or float32");
@@ -410,6 +411,8 @@ extern "C" int afa_bwd(const void* q, const void* k, const void* v, const void* 
   if (B <= 0 || H <= 0 || L <= 0) return set_last_error(AFA_ERR_INVALID, "batch, heads and sequence must be positive");
   if (D <= 0 || D > 256) return set_last_error(AFA_ERR_INVALID, "afa_bwd: head dimension must be in [1, 256]");
   if (valid_len < 0 || valid_len > L) return set_last_error(AFA_ERR_INVALID, "valid_seq_len must be in [1, seq_len]");
+  if (!(sink_omega >= 0.0f) || !std::isfinite(sink_omega))
+    return set_last_error(AFA_ERR_INVALID, "sink_omega must be finite and nonnegative");
   const size_t need = afa_bwd_workspace_bytes(B, H, L, D, dtype);
   if (!workspace || workspace_bytes < need) {
     char msg[160];
@@ -446,7 +449,7 @@ extern "C" int afa_bwd(const void* q, const void* k, const void* v, const void* 
     e = launch_rowdot<__nv_bfloat16, float>(a, s);
     if (e == cudaSuccess)
       e = launch_tc_bwd(q, k, v, g_out, static_cast<const float*>(d_total), static_cast<const float*>(workspace), dq,
-                        dk, dv, B, H, L, D, a.causal, a.valid, a.scale, status, s, &detail);
+                        dk, dv, B, H, L, D, a.causal, a.valid, a.scale, sink_omega, status, s, &detail);
     if (e != cudaSuccess) {
       char msg[256];
       snprintf(msg, sizeof(msg), "afa_bwd tensor-core launch: %s%s%s", cudaGetErrorString(e), detail ? " -- " : "",

@@ -81,7 +81,11 @@ struct BwdTcArgs {
   int* status;
   int L, causal, valid;
   float scale;
+  float sink;  // d_total - sink is a row's weight sum (the tail test)
 };
+
+// True when query row q's weights all lie in the negative tail of rho^8.
+__device__ __forceinline__ bool tail_row(const BwdTcArgs& A, float dtot) { return dtot - A.sink < kTailRowSum; }
 
 struct Bars {
   uint64_t *fix_full, *st_full, *st_empty, *s_full, *x_read, *g_full, *o_full, *drain;
@@ -265,8 +269,11 @@ __device__ __forceinline__ void issue(uint8_t* smem, const Bars& b, uint32_t tme
 // gradients y (dP or dP^T); per-column (dK/dV kernel) or per-row (dQ kernel)
 // 1/d_total and E. Writes packed bf16 W and dS. Element pairs go through the
 // packed fp32x2 instructions (FFMA2 / FMUL2), which halve the issue slots of
-// the map; the one MUFU op per element is the rsqrt.
-template <bool MASK, bool PER_COL>
+// the map; the one MUFU op per element is the rsqrt. EXACT: the reference's
+// branch form of rho (octic_exact2), for chunks that touch a query row whose
+// weights all lie in the negative tail (d_total - sink < kTailRowSum), where
+// the single-MUFU form cancels.
+template <bool MASK, bool PER_COL, bool EXACT>
 __device__ __forceinline__ void grad_chunk(const uint32_t (&x)[32], const uint32_t (&y)[32], uint32_t (&wp)[16],
                                            uint32_t (&dp)[16], float scale, const float* inv_c, const float* e_c,
                                            float inv_r, float e_r, int vis_lim, bool vis_row, int causal,
@@ -277,14 +284,20 @@ __device__ __forceinline__ void grad_chunk(const uint32_t (&x)[32], const uint32
 #pragma unroll
   for (int c = 0; c < 32; c += 2) {
     const float2 s = __fmul2_rn(make_float2(__uint_as_float(x[c]), __uint_as_float(x[c + 1])), sc);
-    const float2 rad = __ffma2_rn(s, s, one);
-    const float2 r = make_float2(rsqrt_approx(rad.x), rsqrt_approx(rad.y));
-    const float2 rho = __ffma2_rn(rad, r, s);
-    const float2 p2 = __fmul2_rn(rho, rho);
-    const float2 p4 = __fmul2_rn(p2, p2);
+    float2 r, p8;
+    if constexpr (EXACT) {
+      p8 = octic_exact2(s, r);
+    } else {
+      const float2 rad = __ffma2_rn(s, s, one);
+      r = make_float2(rsqrt_approx(rad.x), rsqrt_approx(rad.y));
+      const float2 rho = __ffma2_rn(rad, r, s);
+      const float2 p2 = __fmul2_rn(rho, rho);
+      const float2 p4 = __fmul2_rn(p2, p2);
+      p8 = __fmul2_rn(p4, p4);
+    }
     const float2 inv = PER_COL ? make_float2(inv_c[c], inv_c[c + 1]) : make_float2(inv_r, inv_r);
     const float2 ne = PER_COL ? make_float2(-e_c[c], -e_c[c + 1]) : make_float2(-e_r, -e_r);
-    float2 w = __fmul2_rn(__fmul2_rn(p4, p4), inv);
+    float2 w = __fmul2_rn(p8, inv);
     const float2 t = __fadd2_rn(make_float2(__uint_as_float(y[c]), __uint_as_float(y[c + 1])), ne);
     float2 ds = __fmul2_rn(__fmul2_rn(r, w), __fmul2_rn(t, c8));
     if (MASK) {
@@ -339,11 +352,14 @@ __global__ void __launch_bounds__(576, 1)
     for (int it = 0; ok && it < niter; ++it) {
       const int q0 = 128 * (i_first + it);
       const int qc0 = q0 + 32 * g;
+      bool tail;
       {  // 1/d_total and E of this warp's 32 query columns
         const int qi = qc0 + lane;
         const bool in = qi < A.L;
-        vec[lane] = in ? 1.0f / A.dtot[rbase + qi] : 0.0f;
+        const float dt = in ? A.dtot[rbase + qi] : 1.0f;
+        vec[lane] = in ? 1.0f / dt : 0.0f;
         vec[32 + lane] = in ? A.e[rbase + qi] : 0.0f;
+        tail = __any_sync(0xffffffffu, in && tail_row(A, dt));
         __syncwarp();
       }
       const uint32_t yb = T::y(DBY ? (it & 1) : 0) + lane_off + 32 * g;
@@ -362,11 +378,14 @@ __global__ void __launch_bounds__(576, 1)
       const bool need_mask = k0 + 127 >= A.valid || q0 + 127 >= A.L || (A.causal && q0 < k0 + 127);
       // Columns past L read 1/d = 0, which zeroes W and dS; the mask covers
       // invisible keys and causal order.
-      if (need_mask)
-        grad_chunk<true, true>(x, y, wp, dp, A.scale, vec, vec + 32, 0.f, 0.f, A.valid, key < A.L, A.causal, key,
-                               qc0, true);
+      if (tail)
+        grad_chunk<true, true, true>(x, y, wp, dp, A.scale, vec, vec + 32, 0.f, 0.f, A.valid, key < A.L, A.causal,
+                                     key, qc0, true);
+      else if (need_mask)
+        grad_chunk<true, true, false>(x, y, wp, dp, A.scale, vec, vec + 32, 0.f, 0.f, A.valid, key < A.L, A.causal,
+                                      key, qc0, true);
       else
-        grad_chunk<false, true>(x, y, wp, dp, A.scale, vec, vec + 32, 0.f, 0.f, 0, true, 0, 0, 0, true);
+        grad_chunk<false, true, false>(x, y, wp, dp, A.scale, vec, vec + 32, 0.f, 0.f, 0, true, 0, 0, 0, true);
       tmem_st16(tmem + yb, dp);       // dS^T over the chunk's first 16 columns
       tmem_st16(tmem + yb + 16, wp);  // W^T over its last 16
       tmem_st_wait();
@@ -454,8 +473,10 @@ __global__ void __launch_bounds__(576, 1)
     const uint32_t lane_off = static_cast<uint32_t>(sub * 32) << 16;
     const long long rbase = static_cast<long long>(bh) * A.L;
     const bool in = qry < A.L;
-    const float inv = in ? 1.0f / A.dtot[rbase + qry] : 0.0f;
+    const float dt = in ? A.dtot[rbase + qry] : 1.0f;
+    const float inv = in ? 1.0f / dt : 0.0f;
     const float ev = in ? A.e[rbase + qry] : 0.0f;
+    const bool tail = __any_sync(0xffffffffu, in && tail_row(A, dt));
     bool ok = true;
     for (int it = 0; ok && it < niter; ++it) {
       const int kc0 = 128 * it + 32 * g;
@@ -473,11 +494,14 @@ __global__ void __launch_bounds__(576, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(b.x_read);
       const bool need_mask = 128 * it + 127 >= A.valid || (A.causal && 128 * it + 127 > q0);
-      if (need_mask)
-        grad_chunk<true, false>(x, y, wp, dp, A.scale, nullptr, nullptr, inv, ev, A.valid, in, A.causal, qry, kc0,
-                                false);
+      if (tail)
+        grad_chunk<true, false, true>(x, y, wp, dp, A.scale, nullptr, nullptr, inv, ev, A.valid, in, A.causal, qry,
+                                      kc0, false);
+      else if (need_mask)
+        grad_chunk<true, false, false>(x, y, wp, dp, A.scale, nullptr, nullptr, inv, ev, A.valid, in, A.causal, qry,
+                                       kc0, false);
       else
-        grad_chunk<false, false>(x, y, wp, dp, A.scale, nullptr, nullptr, inv, ev, 0, true, 0, 0, 0, false);
+        grad_chunk<false, false, false>(x, y, wp, dp, A.scale, nullptr, nullptr, inv, ev, 0, true, 0, 0, 0, false);
       // dS over the chunk's first 16 dP columns: the A operand of dQ += dS K.
       tmem_st16(tmem + yb, dp);
       tmem_st_wait();
@@ -570,8 +594,9 @@ bool tc_bwd_supported(int dtype, int d) { return dtype == kBF16 && (d == 64 || d
 
 cudaError_t launch_tc_bwd(const void* q, const void* k, const void* v, const void* g_out, const float* d_total,
                           const float* e, void* dq, void* dk, void* dv, int B, int H, int L, int D, int causal,
-                          int valid, float scale, int* status, cudaStream_t stream, const char** detail) {
+                          int valid, float scale, float sink, int* status, cudaStream_t stream, const char** detail) {
   BwdTcArgs A{};
+  A.sink = sink;
   A.dtot = d_total;
   A.e = e;
   A.dq = static_cast<__nv_bfloat16*>(dq);

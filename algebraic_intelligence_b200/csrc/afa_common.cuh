@@ -56,28 +56,19 @@ __device__ __forceinline__ double octic_ref(double s) {
   return k4 * k4;
 }
 
-// Tensor-core path form: rho = (1 + s^2) * rsqrt(1 + s^2) + s in one FMA for
+// Tensor-core fast form: rho = (1 + s^2) * rsqrt(1 + s^2) + s in one FMA for
 // both signs -- the reference's positive branch (pallas_afa.py:46) applied to
-// every s -- with one MUFU op per score. The tensor-core kernel is bound by
-// MUFU/issue throughput, and the conjugate negative branch costs a second MUFU
-// op (a reciprocal) per score, which measured 30-45% slower.
-// Error: with r carrying relative error d (|d| < 2^-22 for rsqrt.approx),
-// rho(s) for s >= 0 has relative error ~ |d|; for s < 0 the sum cancels and the
-// relative error of rho is ~ 2 s^2 |d|, so rho^8 is within 8 * 2 s^2 * 2^-22:
-// below 1.2e-3 (under the bf16 rounding P receives) for s >= -16, where
-// rho(s)^8 <= 1/32^8 ~ 1e-12 of the weight of a score of 0. The result is
-// always finite and >= 0 (an even power), and is 0 below s ~ -4e3 where the
-// true weight is < 1e-31. The reference's form is octic_ref.
-__device__ __forceinline__ float octic_fast(float s) {
-  const float rad = fmaf(s, s, 1.0f);
-  const float rho = fmaf(rad, rsqrt_approx(rad), s);
-  const float k2 = rho * rho;
-  const float k4 = k2 * k2;
-  return k4 * k4;
-}
-
-// The same on a pair of scores with the sm_100 packed FP32 instructions
-// (FFMA2 / FMUL2), halving the issue slots of the FP32 work.
+// every s -- with one MUFU op per score, on a pair of scores with the sm_100
+// packed FP32 instructions (FFMA2 / FMUL2). The tensor-core kernels are bound
+// by MUFU/issue throughput, and the conjugate negative branch costs a second
+// MUFU op (a reciprocal) per score, which measured 30-45% slower.
+// Error: rsqrt.approx has relative error |d| <= 2^-22.9 and 1 + s^2 is rounded
+// once (2^-24), so rho(s) for s >= 0 is within ~2^-22; for s < 0 the sum
+// cancels (rho ~ 1/(2|s|) against terms of size |s|) and the relative error of
+// rho grows to ~ 2 s^2 (|d| + 2^-25), i.e. rho^8 to ~ 2.5e-6 s^2: 6.4e-4 at
+// s = -16, 1% at s = -64, 16% at s = -256. The kernels therefore use this form
+// only where that error cannot reach the result (see kTailChunkSum and
+// kTailRowSum) and octic_exact2 elsewhere.
 __device__ __forceinline__ float2 octic_fast2(float2 s) {
   const float2 rad = __ffma2_rn(s, s, make_float2(1.0f, 1.0f));
   const float2 r = make_float2(rsqrt_approx(rad.x), rsqrt_approx(rad.y));
@@ -86,6 +77,51 @@ __device__ __forceinline__ float2 octic_fast2(float2 s) {
   const float2 k4 = __fmul2_rn(k2, k2);
   return __fmul2_rn(k4, k4);
 }
+
+// The reference's branch form (pallas_afa.py:39-49) on a pair of scores, with
+// hardware approximations: r = rsqrt.approx(1 + s^2), and for s < 0
+// rho = r * rcp.approx(1 - s r), the conjugate that never cancels (1 - s r lies
+// in [1, 2)); for s >= 0 rho = (1 + s^2) r + s. rho is within ~4 ulp for every
+// s, so rho^8 is within ~4e-6 relative -- the negative tail included. Also
+// returns r, which the backward reuses. Two MUFU ops per negative score: the
+// tensor-core kernels run it only on chunks whose weights all lie in the tail.
+__device__ __forceinline__ float2 octic_exact2(float2 s, float2& r) {
+  const float2 rad = __ffma2_rn(s, s, make_float2(1.0f, 1.0f));
+  r = make_float2(rsqrt_approx(rad.x), rsqrt_approx(rad.y));
+  const float2 pos = __ffma2_rn(rad, r, s);
+  const float2 u = __fmul2_rn(s, r);
+  float2 rho;
+  rho.x = s.x < 0.0f ? r.x * rcp_approx(1.0f - u.x) : pos.x;
+  rho.y = s.y < 0.0f ? r.y * rcp_approx(1.0f - u.y) : pos.y;
+  const float2 k2 = __fmul2_rn(rho, rho);
+  const float2 k4 = __fmul2_rn(k2, k2);
+  return __fmul2_rn(k4, k4);
+}
+__device__ __forceinline__ float2 octic_exact2(float2 s) {
+  float2 r;
+  return octic_exact2(s, r);
+}
+
+// When the fast form is exact enough. Errors below are relative to the sum of
+// the weights they are part of; a weighted mean of values (the output) carries
+// at most the same relative error.
+//
+// Per chunk (forward: one query row against 32 keys): if the chunk's weights
+// sum to at least kTailChunkSum (= rho(-15.8)^8), every key at s >= -32
+// carries relative error <= 2.6e-3, and the keys below -32 -- whose errors
+// are larger but whose weights fall as s^-8 -- add at most
+// 32 * 2.6e-3 * (16/32)^8 = 3.3e-4 of the chunk's sum. So a chunk with sum
+// >= kTailChunkSum is within ~3e-3 of exact, under the bf16 rounding of P; a
+// chunk below it is mapped again with octic_exact2.
+constexpr float kTailChunkSum = 1e-12f;
+// Per row (or any set of a row's keys): once the weights sum to at least
+// kTailRowSum (= rho(-4.95)^8), a key at s < -16 adds error at most
+// eps(s) rho(s)^8 <= 6.4e-4 * rho(-16)^8 = 5.8e-16, i.e. 5.8e-8 of the sum, so
+// even 65536 such keys add < 4e-3, and keys at s >= -16 carry <= 6.4e-4 each.
+// The forward therefore checks chunks only until every row of a warp has
+// passed kTailRowSum, and the backward, which knows each row's sum from
+// d_total - sink, takes the exact form for the rows below it.
+constexpr float kTailRowSum = 1e-8f;
 
 // ---------------------------------------------------------------------------
 // Type helpers

@@ -14,7 +14,9 @@
 //     consecutive in memory (fully coalesced); UNROLL independent K and V loads
 //     per lane are in flight before any arithmetic;
 //   * the dot product is reduced across the row's lanes with xor shuffles;
-//     every lane then holds s, maps it and accumulates p*v on its own columns;
+//     every lane then holds s, maps it with the reference's branch form of rho
+//     (octic_ref: exact in the negative tail; its second MUFU op is free in a
+//     kernel bound by HBM) and accumulates p*v on its own columns;
 //   * warp partials combine by xor shuffle, CTA partials through shared memory;
 //   * with more than one split, per-split (numerator, row sum) partials go to a
 //     workspace and a second kernel adds them -- plain addition, since AFA needs
@@ -56,15 +58,6 @@ __device__ __forceinline__ uint4 ldg_stream(const void* p) {
   return r;
 }
 
-template <typename T>
-__device__ __forceinline__ float decode_octic(float s) {
-  if constexpr (sizeof(T) == 2) {
-    return octic_fast(s);
-  } else {
-    return octic_ref(s);
-  }
-}
-
 template <typename T, int D, int UNROLL>
 __global__ void __launch_bounds__(kDecThreads) afa_decode_kernel(const T* __restrict__ q, const T* __restrict__ k,
                                                                  const T* __restrict__ v, T* __restrict__ out,
@@ -82,8 +75,11 @@ __global__ void __launch_bounds__(kDecThreads) afa_decode_kernel(const T* __rest
   const int bh = blockIdx.x;
   const int split = blockIdx.y;
   const int b = bh / H;
+  // Visible prefix of the cache, clamped to [0, lkv]; an empty row gives
+  // output 0 and d_total = sink.
   int len = kv_lens ? kv_lens[b] : kv_len;
   len = len < lkv ? len : lkv;
+  len = len > 0 ? len : 0;
   const int kbeg = split * chunk;
   const int kend = min(len, kbeg + chunk);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -127,7 +123,7 @@ __global__ void __launch_bounds__(kDecThreads) afa_decode_kernel(const T* __rest
 #pragma unroll
       for (int off = LPR / 2; off > 0; off >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, off);
       const int key = base + u * RPW + rsub;
-      float p = decode_octic<T>(dot * scale);
+      float p = octic_ref(dot * scale);
       p = key < kend ? p : 0.f;
       dsum += p;
       const float pr = round_like<T>(p);
@@ -158,7 +154,7 @@ __global__ void __launch_bounds__(kDecThreads) afa_decode_kernel(const T* __rest
       float acc = 0.f;
 #pragma unroll
       for (int w = 0; w < kDecWarps; ++w) acc += s_o[w][c];
-      out[static_cast<long long>(bh) * D + c] = from_acc<T>(acc / denom);
+      out[static_cast<long long>(bh) * D + c] = from_acc<T>(denom > 0.f ? acc / denom : 0.f);
     }
     if (threadIdx.x == 0 && dtot) dtot[bh] = denom;
   } else {
@@ -184,7 +180,7 @@ __global__ void afa_decode_combine_kernel(const float* __restrict__ ws_o, const 
   for (int c = threadIdx.x; c < d; c += blockDim.x) {
     float acc = 0.f;
     for (int s = 0; s < nsplit; ++s) acc += ws_o[(static_cast<long long>(bh) * nsplit + s) * d + c];
-    out[static_cast<long long>(bh) * d + c] = from_acc<T>(acc / den);
+    out[static_cast<long long>(bh) * d + c] = from_acc<T>(den > 0.f ? acc / den : 0.f);
   }
   if (threadIdx.x == 0 && dtot) dtot[bh] = den;
 }

@@ -3,12 +3,11 @@
 //
 // afa_decode takes its split-KV scratch from the caller (sized by
 // afa_decode_workspace_bytes). Some callers have no way to provide it:
-// - code running inside a CUDA graph capture, where a cudaMalloc would break
-//   the capture;
 // - plugin hosts whose device allocator belongs to another runtime and is not
 //   reachable from the plugin (an XLA custom call that was not handed a scratch
 //   buffer, for instance);
-// - serving loops that forbid allocation on the per-token path.
+// - serving loops that forbid allocation on the per-token path, where a
+//   cudaMalloc would synchronise the device and stall every stream.
 // This entry point runs the same kernels with the scratch placed in a
 // fixed-size array in this library's device memory instead.
 //
@@ -22,9 +21,14 @@
 //   streams, or several host threads using one device) race on it; serialise
 //   them on one stream. Each call overwrites every scratch element it later
 //   reads, so nothing needs clearing between calls.
+// - Only shapes that run the split-KV kernels use the array (bf16 with head
+//   dim 64/128/256, f32 with 64/128); other shapes run without scratch.
 // - The first call on a device resolves the array's device address
-//   (cudaGetSymbolAddress) and caches it. Make that first call outside any
+//   (cudaGetSymbolAddress) and caches it. Make that first call before any
 //   stream capture.
+// - The cached address belongs to the device's current context: do not use
+//   the library across cudaDeviceReset (or a reset of the primary context),
+//   after which the address is stale.
 #include <cstdio>
 #include <mutex>
 
@@ -50,7 +54,8 @@ std::mutex g_scratch_mu;
 extern "C" int afa_decode_noalloc(const void* q, const void* k_cache, const void* v_cache, void* out, void* d_total,
                                   int B, int H, int Lkv, int D, int dtype, float sink_omega, const int* kv_lens,
                                   int kv_len, void* stream) {
-  const size_t need = afa_decode_workspace_bytes(B, H, Lkv, D);
+  // Only the split-KV kernels use scratch; afa_decode checks the dtype.
+  const size_t need = afa::decode_fast_supported(dtype, D) ? afa_decode_workspace_bytes(B, H, Lkv, D) : 0;
   if (need > kNoallocScratchBytes) {
     char msg[256];
     snprintf(msg, sizeof(msg),

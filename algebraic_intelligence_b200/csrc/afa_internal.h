@@ -65,7 +65,7 @@ cudaError_t launch_simt_fwd(Launch L, int dtype, cudaStream_t stream, const char
 bool tc_bwd_supported(int dtype, int d);
 cudaError_t launch_tc_bwd(const void* q, const void* k, const void* v, const void* g_out, const float* d_total,
                           const float* e, void* dq, void* dk, void* dv, int B, int H, int L, int D, int causal,
-                          int valid, float scale, int* status, cudaStream_t stream, const char** detail);
+                          int valid, float scale, float sink, int* status, cudaStream_t stream, const char** detail);
 
 cudaError_t launch_finalize(const void* o_acc, const void* d_acc, void* out, void* dtot, long long rows, int d,
                             int dtype, double sink, cudaStream_t stream);

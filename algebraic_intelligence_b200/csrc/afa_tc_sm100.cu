@@ -149,15 +149,17 @@ __host__ __device__ __forceinline__ PairGeom pair_geom(const Launch& L, int cta)
 
 // Octic map of one 32-column chunk of a score row, written back as 16 packed
 // bf16 pairs; returns the chunk's fp32 row sum. MASK selects the per-element
-// visibility test (diagonal and partial tiles only).
-template <bool MASK>
+// visibility test (diagonal and partial tiles only); EXACT the reference's
+// branch form of rho (octic_exact2) instead of the single-MUFU one.
+template <bool MASK, bool EXACT>
 __device__ __forceinline__ float map_chunk(const uint32_t (&sv)[32], uint32_t (&pk)[16], float scale, int key0,
                                            int lim, int causal, int kpos0, int qpos) {
   float2 acc = make_float2(0.f, 0.f);
   const float2 sc = make_float2(scale, scale);
 #pragma unroll
   for (int e = 0; e < 32; e += 2) {
-    float2 p = octic_fast2(__fmul2_rn(make_float2(__uint_as_float(sv[e]), __uint_as_float(sv[e + 1])), sc));
+    const float2 s = __fmul2_rn(make_float2(__uint_as_float(sv[e]), __uint_as_float(sv[e + 1])), sc);
+    float2 p = EXACT ? octic_exact2(s) : octic_fast2(s);
     if (MASK) {
       const int c0 = key0 + e, c1 = c0 + 1;
       const bool v0 = (c0 < lim) && (!causal || kpos0 + c0 <= qpos);
@@ -169,6 +171,55 @@ __device__ __forceinline__ float map_chunk(const uint32_t (&sv)[32], uint32_t (&
     pk[e >> 1] = pack_bf16x2(p.x, p.y);
   }
   return acc.x + acc.y;
+}
+
+// Maps the 32-column chunk of TMEM scores at s_tm into pk and returns its row
+// sum with the single-MUFU form. CHECK: a warp with a lane that sees a key
+// and whose chunk weights sum below kTailChunkSum (every score of that row
+// chunk deep in the negative tail, where the fast form cancels) maps the
+// chunk again with the exact form, from the scores still in TMEM.
+template <bool CHECK>
+__device__ __forceinline__ float map_chunk_tmem(uint32_t s_tm, uint32_t (&pk)[16], bool need_mask, float scale,
+                                                int key0, int lim, int causal, int kpos0, int qpos) {
+  uint32_t sv[32];
+  tmem_ld32(s_tm, sv);
+  tmem_ld_wait();
+  float part = need_mask ? map_chunk<true, false>(sv, pk, scale, key0, lim, causal, kpos0, qpos)
+                         : map_chunk<false, false>(sv, pk, scale, key0, lim, causal, kpos0, qpos);
+  if constexpr (CHECK) {
+    // Visible keys of a chunk form a prefix, so it sees one iff it sees key0.
+    const bool sees = !need_mask || (key0 < lim && (!causal || kpos0 + key0 <= qpos));
+    if (__any_sync(0xffffffffu, sees && part < kTailChunkSum)) {
+      tmem_ld32(s_tm, sv);
+      tmem_ld_wait();
+      part = need_mask ? map_chunk<true, true>(sv, pk, scale, key0, lim, causal, kpos0, qpos)
+                       : map_chunk<false, true>(sv, pk, scale, key0, lim, causal, kpos0, qpos);
+    }
+  }
+  return part;
+}
+
+// Maps one key tile's two 32-column chunks of this warp (columns
+// [key_base, key_base + 64)), stores P and adds the chunk sums to dsum. The
+// chunk check (CHECK) is needed only while the warp holds a row whose weights
+// so far sum below kTailRowSum: past that, the errors of later tail chunks are
+// bounded by the row sum they add to (see kTailRowSum), so the loop drops the
+// check once every lane has passed it -- after the first key tile, for all
+// but rows wholly in the tail. (The checked path's code alone, never run,
+// measured about 1% on short prefills; the check itself adds little.)
+template <bool CHECK>
+__device__ __forceinline__ void map_tile(uint32_t s_base, int key_base, bool need_mask, float scale, int lim,
+                                         int causal, int kpos0, int qpos, float& dsum) {
+#pragma unroll 1
+  for (int c = 0; c < 2; ++c) {
+    const int key0 = key_base + 32 * c;
+    const uint32_t s_tm = s_base + key0;
+    uint32_t pk[16];
+    const float part = map_chunk_tmem<CHECK>(s_tm, pk, need_mask, scale, key0, lim, causal, kpos0, qpos);
+    // P of these 32 keys -> the first 16 of the 32 columns just read.
+    tmem_st16(s_tm, pk);
+    dsum += part;
+  }
 }
 
 // Transposes NCH x NCH blocks of float4 chunks within groups of NCH lanes:
@@ -411,6 +462,7 @@ __global__ void __launch_bounds__(576, 1)
     const uint32_t lane_off = static_cast<uint32_t>(sub * 32) << 16;
     const float scale = L.scale;
     float dsum = 0.f;
+    bool tail_check = true;  // warp-uniform: some row's weights so far < kTailRowSum
     bool ok = true;
     const int nmap = mt ? n1 : n0;
     for (int t = 0; t < nmap && ok; ++t) {
@@ -422,19 +474,12 @@ __global__ void __launch_bounds__(576, 1)
       const int qfirst = P.q.pos0 + r0 + 128 * mt;
       const int qpos = qfirst + row;
       const bool need_mask = kt.lim < 128 || (L.causal && kt.pos + 127 > qfirst);
-#pragma unroll 1
-      for (int c = 0; c < 2; ++c) {
-        const int key0 = 64 * mh + 32 * c;
-        const uint32_t s_tm = tmem + C::s_col(mt) + lane_off + key0;
-        uint32_t sv[32];
-        uint32_t pk[16];
-        tmem_ld32(s_tm, sv);
-        tmem_ld_wait();
-        const float part = need_mask ? map_chunk<true>(sv, pk, scale, key0, kt.lim, L.causal, kt.pos, qpos)
-                                     : map_chunk<false>(sv, pk, scale, key0, kt.lim, L.causal, kt.pos, qpos);
-        // P of these 32 keys -> the first 16 of the 32 columns just read.
-        tmem_st16(s_tm, pk);
-        dsum += part;
+      const uint32_t s_base = tmem + C::s_col(mt) + lane_off;
+      if (tail_check) {
+        map_tile<true>(s_base, 64 * mh, need_mask, scale, kt.lim, L.causal, kt.pos, qpos, dsum);
+        tail_check = __any_sync(0xffffffffu, dsum < kTailRowSum);
+      } else {
+        map_tile<false>(s_base, 64 * mh, need_mask, scale, kt.lim, L.causal, kt.pos, qpos, dsum);
       }
       // Every lane's P stores are complete (wait::st) and ordered before the
       // warp's single arrive.
@@ -966,6 +1011,7 @@ __global__ void __launch_bounds__(576, 1)
       const int e0 = sg.t1 < G.n0 ? sg.t1 : G.n0;
       const int tend = mt ? sg.t1 : e0;  // this warp's tile: key tiles [sg.t0, tend)
       float dsum = 0.f;
+      bool tail_check = true;  // warp-uniform: some row's weights so far < kTailRowSum
       for (int t = sg.t0; t < tend && ok; ++t) {
         const KvTile kt = kv_tile(P, G.cnt1_0, t);
         ok = mbar_wait(s_full + mt, sc & 1, L.status, kDevTimeoutSoftmax);
@@ -976,18 +1022,12 @@ __global__ void __launch_bounds__(576, 1)
         const int qfirst = P.q.pos0 + G.r0 + 128 * mt;
         const int qpos = qfirst + row;
         const bool need_mask = kt.lim < 128 || (L.causal && kt.pos + 127 > qfirst);
-#pragma unroll 1
-        for (int c = 0; c < 2; ++c) {
-          const int key0 = 64 * mh + 32 * c;
-          const uint32_t s_tm = tmem + C::s_col(mt) + lane_off + key0;
-          uint32_t sv[32];
-          uint32_t pk[16];
-          tmem_ld32(s_tm, sv);
-          tmem_ld_wait();
-          const float part = need_mask ? map_chunk<true>(sv, pk, scale, key0, kt.lim, L.causal, kt.pos, qpos)
-                                       : map_chunk<false>(sv, pk, scale, key0, kt.lim, L.causal, kt.pos, qpos);
-          tmem_st16(s_tm, pk);
-          dsum += part;
+        const uint32_t s_base = tmem + C::s_col(mt) + lane_off;
+        if (tail_check) {
+          map_tile<true>(s_base, 64 * mh, need_mask, scale, kt.lim, L.causal, kt.pos, qpos, dsum);
+          tail_check = __any_sync(0xffffffffu, dsum < kTailRowSum);
+        } else {
+          map_tile<false>(s_base, 64 * mh, need_mask, scale, kt.lim, L.causal, kt.pos, qpos, dsum);
         }
         tmem_st_wait();
         tc_fence_before();

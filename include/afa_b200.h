@@ -161,14 +161,19 @@ AFA_API int afa_ring_pull(void* dst, const void* src, size_t bytes, void* stream
  * :555-575): dq, dk, dv of sum(out * g_out) for out = afa_fwd(q, k, v).
  *   q, k, v, out, g_out, dq, dk, dv  (B, H, L, D) in `dtype` (bf16, f32, f64)
  *   d_total   (B, H, L) from afa_fwd: row sum + sink, float32 (float64 for f64)
+ *   sink_omega the forward's sink (tiled_afa_backward's sink_omega argument).
+ *             The gradient math uses the sink only through d_total, as in the
+ *             reference (:429); d_total - sink_omega, a row's weight sum, tells
+ *             the bf16 tensor-core kernels which rows lie wholly in the
+ *             negative tail of rho^8 and need its cancellation-free branch.
  *   causal, valid_len as afa_fwd (valid_len 0 = L)
  *   workspace afa_bwd_workspace_bytes(B, H, L, D, dtype) bytes of device
  *             scratch (the per-row E = sum(g_out * out)), caller-owned.
- * The sink enters only through d_total, as in the reference (:429).
  */
 AFA_API int afa_bwd(const void* q, const void* k, const void* v, const void* out, const void* d_total,
                     const void* g_out, void* dq, void* dk, void* dv, int B, int H, int L, int D, int dtype,
-                    int causal, int valid_len, void* workspace, size_t workspace_bytes, void* stream);
+                    float sink_omega, int causal, int valid_len, void* workspace, size_t workspace_bytes,
+                    void* stream);
 AFA_API size_t afa_bwd_workspace_bytes(int B, int H, int L, int D, int dtype);
 
 /*
@@ -199,8 +204,9 @@ AFA_API int afa_ago_rotate(const void* q, const void* k, void* q_out, void* k_ou
  *   q           (B, H, D) -- one token per (batch, head)
  *   k_cache, v_cache  (B, H, Lkv, D)
  *   out         (B, H, D); d_total (B, H) float32, may be NULL.
- *   kv_lens     optional device int32[B]: visible cache length per batch row;
- *               NULL uses kv_len for all rows (0 = Lkv).
+ *   kv_lens     optional device int32[B]: visible cache length per batch row,
+ *               clamped to [0, Lkv]; a row of length 0 gives output 0 and
+ *               d_total = sink_omega. NULL uses kv_len for all rows (0 = Lkv).
  *   workspace   device scratch of afa_decode_workspace_bytes(B, H, Lkv, D)
  *               bytes (may be NULL when that size is 0).
  * AFA_BF16 (D in 64/128/256) and AFA_F32 (D in 64/128) use the split-KV
@@ -215,15 +221,16 @@ AFA_API size_t afa_decode_workspace_bytes(int B, int H, int Lkv, int D);
 /*
  * Allocation-free decode step. No counterpart in the reference: it is
  * afa_decode for callers that cannot hand over device scratch memory --
- * code inside a CUDA graph capture, plugin hosts whose allocator belongs to
- * another runtime, serving loops that forbid allocation per token. Same
- * arguments and results as afa_decode minus the workspace. The split-KV
- * scratch instead lives in a fixed 1 MiB array that every GPU loading the
- * library keeps until exit. Shapes needing more scratch than that
- * (afa_decode_workspace_bytes > 1 MiB) return AFA_ERR_INVALID. All calls
+ * plugin hosts whose allocator belongs to another runtime, serving loops that
+ * forbid allocation per token. Same arguments and results as afa_decode minus
+ * the workspace. The split-KV scratch instead lives in a fixed 1 MiB array
+ * that every GPU loading the library keeps until exit. Shapes whose split-KV
+ * scratch exceeds that (afa_decode_workspace_bytes > 1 MiB for a dtype and
+ * head dim afa_decode streams with split-KV) return AFA_ERR_INVALID. All calls
  * share the array, so calls that overlap on the GPU race; serialise them on
  * one stream. The first call on a device resolves the array's device address
- * (cudaGetSymbolAddress); make it outside any stream capture.
+ * (cudaGetSymbolAddress); make it before any stream capture. That address is
+ * cached for the process: do not use the library across cudaDeviceReset.
  */
 AFA_API int afa_decode_noalloc(const void* q, const void* k_cache, const void* v_cache, void* out, void* d_total,
                                int B, int H, int Lkv, int D, int dtype, float sink_omega, const int* kv_lens,

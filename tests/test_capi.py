@@ -117,11 +117,16 @@ def test_backward_argument_checks():
     ptrs = [1] * 9
     assert lib.afa_bwd_workspace_bytes(2, 3, 100, 64, _lib.AFA_F32) == 2 * 3 * 100 * 4
     assert lib.afa_bwd_workspace_bytes(2, 3, 100, 64, _lib.AFA_F64) == 2 * 3 * 100 * 8
-    assert lib.afa_bwd(*ptrs, 1, 1, 64, 64, _lib.AFA_F16, 0, 0, 1, 1 << 20, None) == _lib.AFA_ERR_DTYPE
-    assert lib.afa_bwd(None, *ptrs[1:], 1, 1, 64, 64, _lib.AFA_BF16, 0, 0, 1, 1 << 20, None) == _lib.AFA_ERR_INVALID
-    assert lib.afa_bwd(*ptrs, 1, 1, 64, 512, _lib.AFA_BF16, 0, 0, 1, 1 << 20, None) == _lib.AFA_ERR_INVALID
-    assert lib.afa_bwd(*ptrs, 1, 1, 64, 64, _lib.AFA_BF16, 0, 65, 1, 1 << 20, None) == _lib.AFA_ERR_INVALID
-    assert lib.afa_bwd(*ptrs, 1, 1, 64, 64, _lib.AFA_BF16, 0, 0, 1, 16, None) == _lib.AFA_ERR_INVALID
+    assert lib.afa_bwd(*ptrs, 1, 1, 64, 64, _lib.AFA_F16, 0.5, 0, 0, 1, 1 << 20, None) == _lib.AFA_ERR_DTYPE
+    assert lib.afa_bwd(None, *ptrs[1:], 1, 1, 64, 64, _lib.AFA_BF16, 0.5, 0, 0, 1, 1 << 20,
+                       None) == _lib.AFA_ERR_INVALID
+    assert lib.afa_bwd(*ptrs, 1, 1, 64, 512, _lib.AFA_BF16, 0.5, 0, 0, 1, 1 << 20, None) == _lib.AFA_ERR_INVALID
+    assert lib.afa_bwd(*ptrs, 1, 1, 64, 64, _lib.AFA_BF16, 0.5, 0, 65, 1, 1 << 20, None) == _lib.AFA_ERR_INVALID
+    for bad_sink in (-1.0, float("inf"), float("nan")):
+        assert lib.afa_bwd(*ptrs, 1, 1, 64, 64, _lib.AFA_BF16, bad_sink, 0, 0, 1, 1 << 20,
+                           None) == _lib.AFA_ERR_INVALID
+        assert b"sink_omega" in lib.afa_last_error()
+    assert lib.afa_bwd(*ptrs, 1, 1, 64, 64, _lib.AFA_BF16, 0.5, 0, 0, 1, 16, None) == _lib.AFA_ERR_INVALID
     assert b"workspace" in lib.afa_last_error()
 
 

@@ -93,6 +93,30 @@ def test_decode_kv_lens(dtype):
     assert orc.rel_err(host64(y2), ref2) <= TOL[dtype]
 
 
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+@pytest.mark.parametrize("sink", [0.0, 0.5])
+def test_decode_empty_and_clamped_rows(dtype, sink):
+    """Per-batch lengths on the device are clamped to [0, Lkv]: a row of length
+    0 (or less) gives output 0 and d_total = sink -- no 0/0 with sink 0 -- and
+    a length past the cache reads the whole cache. Host lengths outside
+    [0, Lkv] are rejected."""
+    rng = np.random.default_rng(22)
+    b, h, lkv, d = 4, 2, 700, 128
+    q = to_dev(rng.normal(size=(b, h, d)), dtype)
+    k = to_dev(rng.normal(size=(b, h, lkv, d)), dtype)
+    v = to_dev(rng.normal(size=(b, h, lkv, d)), dtype)
+    lens = torch.tensor([0, -5, 300, 5000], dtype=torch.int32, device="cuda")
+    y, den = afa.afa_decode(q, k, v, sink_omega=sink, kv_len=lens, return_denominator=True)
+    yh, dh = host64(y), host64(den)
+    assert np.isfinite(yh).all()
+    assert np.all(yh[:2] == 0.0) and np.all(dh[:2] == sink)
+    ref, rden = orc.decode(host64(q[2:]), host64(k[2:]), host64(v[2:]), sink=sink, kv_len=[300, lkv])
+    assert orc.rel_err(yh[2:], ref) <= TOL[dtype]
+    assert orc.rel_err(dh[2:], rden) <= 1e-5
+    with pytest.raises(ValueError, match="kv_len"):
+        afa.afa_decode(q, k, v, kv_len=torch.tensor([1, 2, -1, 3], dtype=torch.int32))
+
+
 def test_decode_matches_prefill_row():
     """A decode step equals the forward of a single query row over the cache."""
     rng = np.random.default_rng(5)
