@@ -132,6 +132,8 @@ def main(root: str) -> None:
 
 
 if __name__ == "__main__":
-    root = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
+    if len(sys.argv) != 2:
+        sys.exit("usage: python tests/golden/make_golden.py <path to a checkout of the reference repository>")
+    root = sys.argv[1]
     main(root)
     make_ago(Path(root))
