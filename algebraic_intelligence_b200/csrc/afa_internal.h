@@ -60,6 +60,7 @@ inline int assign_ctas(Launch& L, int rows_per_cta) {
 // message on failure.
 bool tc_fwd_supported(int dtype, int d);
 cudaError_t launch_tc_fwd(Launch L, int dtype, cudaStream_t stream, const char** detail);
+
 cudaError_t launch_simt_fwd(Launch L, int dtype, cudaStream_t stream, const char** detail);
 
 bool tc_bwd_supported(int dtype, int d);
