@@ -141,16 +141,48 @@ __device__ __forceinline__ float map_chunk_tmem(uint32_t s_tm, uint32_t (&pk)[16
 // check once every lane has passed it -- after the first key tile, for all
 // but rows wholly in the tail. (The checked path's code alone, never run,
 // measured about 1% on short prefills; the check itself adds little.)
+//
+// In a masked tile (need_mask: the diagonal of a causal launch, or a partial
+// key tile) each chunk is classed for the warp's 32 rows as a whole (the rows
+// are consecutive, so the visible keys of row i are a prefix no shorter than
+// row i-1's): a chunk no row of the warp sees gets P = 0 without loading or
+// mapping its scores, a chunk every row sees in full takes the unmasked map,
+// and only the chunks crossing the diagonal (or the valid length) run the
+// per-element mask. The unmasked tiles keep a loop of their own: with the
+// classes inside one shared loop the long-sequence launch measured 1-2% slower.
 template <bool CHECK>
 __device__ __forceinline__ void map_tile(uint32_t s_base, int key_base, bool need_mask, float scale, int lim,
                                          int causal, int kpos0, int qpos, float& dsum) {
+  if (!need_mask) {
+#pragma unroll 1
+    for (int c = 0; c < 2; ++c) {
+      const int key0 = key_base + 32 * c;
+      const uint32_t s_tm = s_base + key0;
+      uint32_t pk[16];
+      const float part = map_chunk_tmem<CHECK>(s_tm, pk, false, scale, key0, lim, causal, kpos0, qpos);
+      // P of these 32 keys -> the first 16 of the 32 columns just read.
+      tmem_st16(s_tm, pk);
+      dsum += part;
+    }
+    return;
+  }
+  // Last key index (tile-relative) the warp's first / last row sees.
+  const int row_first = qpos - static_cast<int>(threadIdx.x & 31);
+  const int vis_first = causal ? row_first - kpos0 : 0x7fffffff;
+  const int vis_last = causal ? row_first + 31 - kpos0 : 0x7fffffff;
 #pragma unroll 1
   for (int c = 0; c < 2; ++c) {
     const int key0 = key_base + 32 * c;
     const uint32_t s_tm = s_base + key0;
     uint32_t pk[16];
-    const float part = map_chunk_tmem<CHECK>(s_tm, pk, need_mask, scale, key0, lim, causal, kpos0, qpos);
-    // P of these 32 keys -> the first 16 of the 32 columns just read.
+    float part = 0.f;
+    if (key0 >= lim || key0 > vis_last) {  // no row of the warp sees a key of the chunk
+#pragma unroll
+      for (int i = 0; i < 16; ++i) pk[i] = 0u;
+    } else {
+      const bool full = key0 + 31 < lim && key0 + 31 <= vis_first;
+      part = map_chunk_tmem<CHECK>(s_tm, pk, !full, scale, key0, lim, causal, kpos0, qpos);
+    }
     tmem_st16(s_tm, pk);
     dsum += part;
   }
