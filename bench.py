@@ -145,6 +145,9 @@ def dist_setup(n_gpus):
     if world > 1:
         import torch.distributed as dist
         os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        # Each rank's NCCL communicator reports its rank and size at init.
+        os.environ.setdefault("NCCL_DEBUG", "INFO")
+        os.environ.setdefault("NCCL_DEBUG_SUBSYS", "INIT")
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local))
     return rank, world, local
@@ -257,6 +260,9 @@ def run_ring(args, rank, world, peaks, traffic):
         den = torch.empty((b, h, s, 1), dtype=torch.float32, device="cuda")
         out = torch.empty_like(q0)
         exchange = get_exchange(q0.shape, q0.dtype, q0.device)   # the one distributed_ring_afa uses
+        phases = PhaseTimer()
+        timed_exchange = TimedExchange(exchange, phases)
+        live = [i for i, hp in enumerate(hops) if hp.problems]
 
         def step(i, kt):
             q, k, v = sets[i % 2]
@@ -264,9 +270,14 @@ def run_ring(args, rank, world, peaks, traffic):
             def compute(hop, kk, vv):
                 f = lambda: hop_forward(q, kk, vv, hop.problems, True, hop.mode, o_acc=o_acc,  # noqa: E731
                                         d_acc=d_acc, out=out, d_total=den, sink_omega=0.5)
-                kt.around(f) if kt else f()
+                if kt is None:
+                    f()
+                    return
+                j = next(n for n, hp in enumerate(hops) if hp is hop)
+                name = "hop0_store" if j == live[0] else ("hop_last_finalize" if j == live[-1] else "hop_accumulate")
+                phases.around(name, lambda: kt.around(f))
 
-            ring_loop(k, v, hops, compute, exchange)
+            ring_loop(k, v, hops, compute, timed_exchange if kt is not None else exchange)
 
     ms, kt = timed(step, args.steps, args.warmup, world)
     value = flops * args.steps / (ms / 1e3) / 1e12
@@ -287,8 +298,59 @@ def run_ring(args, rank, world, peaks, traffic):
                      "traffic": tr, "peak_source": peaks["source"] + " bf16_tflops (burst)",
                      "launch_ms": kernel_ms, "flops_per_launch": per_launch_flops},
     }
+    if world > 1:
+        # Where a ring step's time goes, max over ranks (ms per step; per launch
+        # for the hop kernels): the first hop's STORE kernel, the accumulate
+        # hops' kernels, the last hop (accumulate + divide), the publish (K/V
+        # copy into the IPC buffer + the first barrier) and the close (joining
+        # the copy stream + the second barrier).
+        res["hop_breakdown"] = {k: max_over_ranks(v, world) for k, v in phases.summary(args.steps).items()}
     del sets
     return res
+
+
+class PhaseTimer:
+    """CUDA-event pairs per named phase, on the current stream."""
+
+    def __init__(self):
+        self.pairs = {}
+
+    def around(self, name, fn):
+        import torch
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        r = fn()
+        e.record()
+        self.pairs.setdefault(name, []).append((s, e))
+        return r
+
+    def summary(self, steps):
+        out = {}
+        for name, pairs in sorted(self.pairs.items()):
+            tot = sum(s.elapsed_time(e) for s, e in pairs)
+            out[f"{name}_ms_per_step"] = tot / steps
+            if name.startswith("hop"):
+                out[f"{name}_ms_per_launch"] = tot / len(pairs)
+        return out
+
+
+class TimedExchange:
+    """The ring's exchange with its publish and close phases timed."""
+
+    def __init__(self, ex, phases):
+        self.ex, self.phases, self.rank = ex, phases, ex.rank
+
+    def publish(self, k, v):
+        return self.phases.around("publish_copy_and_barrier", lambda: self.ex.publish(k, v))
+
+    def pull(self, src, slot):
+        return self.ex.pull(src, slot)
+
+    def ready(self, token):
+        return self.ex.ready(token)
+
+    def finish(self):
+        self.phases.around("close_join_and_barrier", self.ex.finish)
 
 
 def run_ring_e2e(args, rank, world):
@@ -637,6 +699,7 @@ def main():
             "tok_per_s": ring["tok_per_s"],
             "gpu_launches": ring["gpu_launches"],
             "roofline": ring["roofline"],
+            **({"hop_breakdown": ring["hop_breakdown"]} if "hop_breakdown" in ring else {}),
             "e2e": e2e,
             "clocks": clk,
             "device_status": status,
