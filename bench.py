@@ -37,6 +37,13 @@ import sys
 import time
 from pathlib import Path
 
+# Under torch.distributed.run (N > 1) each rank's NCCL communicator reports its
+# rank and size when it is created (NCCL's INIT log lines; rank 0's JSON result
+# is still one line of its own). NCCL reads these once, before torch is imported.
+if int(os.environ.get("WORLD_SIZE", "1")) > 1:
+    os.environ.setdefault("NCCL_DEBUG", "INFO")
+    os.environ.setdefault("NCCL_DEBUG_SUBSYS", "INIT")
+
 ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
@@ -145,9 +152,6 @@ def dist_setup(n_gpus):
     if world > 1:
         import torch.distributed as dist
         os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
-        # Each rank's NCCL communicator reports its rank and size at init.
-        os.environ.setdefault("NCCL_DEBUG", "INFO")
-        os.environ.setdefault("NCCL_DEBUG_SUBSYS", "INIT")
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local))
     return rank, world, local
