@@ -54,6 +54,7 @@ CFG3 = dict(B=2, H=32, L=4096, D=128)
 CFG2 = dict(B=4, H=16, L=2048, D=128)
 DEC = dict(B=64, H=32, L=8192, D=128)
 DEC_SMALL = dict(B=8, H=32, L=8192, D=128)  # profiling size (about 1 GB per input set)
+SUB_IDLE_S = 0.5  # idle before each short sub-workload run
 
 
 def causal_flops(B, H, L, D, **_):
@@ -216,6 +217,26 @@ def timed(step, steps, warmup, world):
     return max_over_ranks(ms, world), kt
 
 
+def kernel_ms(launch, steps, warmup=3):
+    """Mean device time (ms) of one launch: `steps` back-to-back launches
+    through the C ABI with prepared arguments, bracketed by one CUDA event pair
+    on the launching stream. For launches shorter than the host work of an API
+    call (tens of microseconds of Python), events around each call would count
+    the GPU idling while the host prepares the next one; here the stream stays
+    busy, so the pair measures the kernels alone."""
+    import torch
+    for i in range(warmup):
+        launch(i)
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for i in range(steps):
+        launch(i)
+    b.record()
+    torch.cuda.synchronize()
+    return a.elapsed_time(b) / steps
+
+
 # ---------------------------------------------------------------------------
 # workloads
 # ---------------------------------------------------------------------------
@@ -285,9 +306,9 @@ def run_ring(args, rank, world, peaks, traffic):
 
     ms, kt = timed(step, args.steps, args.warmup, world)
     value = flops * args.steps / (ms / 1e3) / 1e12
-    kernel_ms = kt.mean_ms()
+    launch_ms = kt.mean_ms()
     per_launch_flops = flops / world / launches_per_step
-    achieved = per_launch_flops / (kernel_ms / 1e3) / 1e12
+    achieved = per_launch_flops / (launch_ms / 1e3) / 1e12
     tr = traffic.get("ring_n1" if world == 1 else f"ring_n{world}")
     res = {
         "value": value,
@@ -300,7 +321,7 @@ def run_ring(args, rank, world, peaks, traffic):
                      "afa_tc_fwd_kernel<128> (first hop) / afa_tc_sk_kernel<128> (other hops)", "achieved": achieved,
                      "peak": peaks["bf16_tflops"], "unit": "TFLOP/s", "frac": achieved / peaks["bf16_tflops"],
                      "traffic": tr, "peak_source": peaks["source"] + " bf16_tflops (burst)",
-                     "launch_ms": kernel_ms, "flops_per_launch": per_launch_flops},
+                     "launch_ms": launch_ms, "flops_per_launch": per_launch_flops},
     }
     if world > 1:
         # Where a ring step's time goes, max over ranks (ms per step; per launch
@@ -439,10 +460,20 @@ def run_prefill(cfg, args, peaks, outliers=False):
 
     steps = max(args.steps, 10)
     ms, kt = timed(step, steps, max(args.warmup, 3), 1)
-    kms = kt.mean_ms()
+    from algebraic_intelligence_b200 import _lib
+    lib = _lib.load()
+    outs = [(torch.empty_like(q), torch.empty((B, H, L), dtype=torch.float32, device=q.device)) for q, _, _ in sets]
+    stream = _lib.stream_ptr(torch.device("cuda", torch.cuda.current_device()))
+
+    def launch(i):
+        (q, k, v), (o, d) = sets[i % 2], outs[i % 2]
+        _lib.check(lib.afa_fwd(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), d.data_ptr(), B, H, L, D,
+                               _lib.AFA_BF16, 0.5, 1, 0, stream), "afa_fwd")
+
+    kms = kernel_ms(launch, steps)
     ach = flops / (kms / 1e3) / 1e12
     return {"value": flops * steps / (ms / 1e3) / 1e12, "unit": UNIT, "ms_per_step": ms / steps,
-            "flops": flops,
+            "flops": flops, "api_call_ms": kt.mean_ms(), "kernel_ms": kms,
             "roofline": {"bound": "tensor", "achieved": ach, "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
                          "frac": ach / peaks["bf16_tflops"], "peak_source": peaks["source"] + " bf16_tflops"}}
 
@@ -471,10 +502,24 @@ def run_backward(cfg, args, peaks):
 
     steps = max(args.steps, 10)
     ms, kt = timed(step, steps, max(args.warmup, 3), 1)
-    kms = kt.mean_ms()
+    from algebraic_intelligence_b200 import _lib
+    lib = _lib.load()
+    need = lib.afa_bwd_workspace_bytes(B, H, L, D, _lib.AFA_BF16)
+    ws = torch.empty(max(need, 1), dtype=torch.uint8, device="cuda")
+    grads = [tuple(torch.empty_like(q) for _ in range(3)) for q, *_ in sets]
+    dens = [den.reshape(B, H, L).contiguous() for *_, den, _ in sets]
+    stream = _lib.stream_ptr(torch.device("cuda", torch.cuda.current_device()))
+
+    def launch(i):
+        (q, k, v, out, _, g), den, (dq, dk, dv) = sets[i % 2], dens[i % 2], grads[i % 2]
+        _lib.check(lib.afa_bwd(q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), den.data_ptr(),
+                               g.data_ptr(), dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), B, H, L, D, _lib.AFA_BF16,
+                               0.5, 1, 0, ws.data_ptr(), need, stream), "afa_bwd")
+
+    kms = kernel_ms(launch, steps)
     ach = flops / (kms / 1e3) / 1e12
     return {"value": flops * steps / (ms / 1e3) / 1e12, "unit": UNIT, "ms_per_step": ms / steps,
-            "flops": flops, "kernels_per_step": 3,
+            "flops": flops, "kernels_per_step": 3, "api_call_ms": kt.mean_ms(), "kernel_ms": kms,
             "roofline": {"bound": "tensor", "achieved": ach, "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
                          "frac": ach / peaks["bf16_tflops"], "peak_source": peaks["source"] + " bf16_tflops"}}
 
@@ -500,10 +545,6 @@ def run_ago(cfg, args, peaks):
 
     steps = max(args.steps, 10)
     ms, kt = timed(step, steps, max(args.warmup, 3), 1)
-    # The kernel alone: at this size one launch (about 40 us) is shorter than
-    # the host work of an API call, so events around each call would count host
-    # time. Back-to-back launches through the C ABI with prepared arguments keep
-    # the stream busy; one event pair brackets them.
     from algebraic_intelligence_b200 import _lib
     lib = _lib.load()
     c, s = rot.c.contiguous(), rot.s.contiguous()
@@ -516,16 +557,7 @@ def run_ago(cfg, args, peaks):
         _lib.check(lib.afa_ago_rotate(q.data_ptr(), k.data_ptr(), qo.data_ptr(), ko.data_ptr(), c.data_ptr(),
                                       s.data_ptr(), tcode, B * H * L, D, L, 1, code, stream), "afa_ago_rotate")
 
-    for i in range(3):
-        launch(i)
-    torch.cuda.synchronize()
-    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    a.record()
-    for i in range(steps):
-        launch(i)
-    b.record()
-    torch.cuda.synchronize()
-    kms = a.elapsed_time(b) / steps
+    kms = kernel_ms(launch, steps)
     ach = nbytes / (kms / 1e3) / 1e9
     return {"value": nbytes * steps / (ms / 1e3) / 1e9, "unit": "GB/s", "ms_per_step": ms / steps,
             "bytes": nbytes, "api_call_ms": kt.mean_ms(), "kernel_ms": kms,
@@ -683,11 +715,16 @@ def main():
     e2e = run_ring_e2e(args, rank, world)
     sub = {}
     if world == 1:
-        sub["prefill_config3_L4096"] = run_prefill(CFG3, args, peaks)
-        sub["prefill_config2_L2048_outliers"] = run_prefill(CFG2, args, peaks, outliers=True)
-        sub["decode_config4"] = run_decode(args, peaks)
-        sub["backward_config3_L4096"] = run_backward(CFG3, args, peaks)
-        sub["ago_rotate_config3_shape"] = run_ago(CFG3, args, peaks)
+        # Each of these short runs starts from an idle GPU (SUB_IDLE_S), not in
+        # the power state the headline's long run at the power cap left behind.
+        for name, fn in (("prefill_config3_L4096", lambda: run_prefill(CFG3, args, peaks)),
+                         ("prefill_config2_L2048_outliers", lambda: run_prefill(CFG2, args, peaks, outliers=True)),
+                         ("decode_config4", lambda: run_decode(args, peaks)),
+                         ("backward_config3_L4096", lambda: run_backward(CFG3, args, peaks)),
+                         ("ago_rotate_config3_shape", lambda: run_ago(CFG3, args, peaks))):
+            torch.cuda.synchronize()
+            time.sleep(SUB_IDLE_S)
+            sub[name] = fn()
     status = _lib.device_status(torch.device("cuda", local))
     if rank == 0:
         line = {
