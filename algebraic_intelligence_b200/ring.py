@@ -137,7 +137,8 @@ class KVExchange:
     """How the hops of one ring call obtain their K/V shards.
 
     ``ring_loop`` drives it: ``publish`` makes this rank's shard readable by
-    every rank of the ring and returns it as a (2, B, H, S, D) tensor;
+    every rank of the ring and returns the local K and V that hop 0 reads
+    (anything indexable as [0] = K, [1] = V);
     ``pull(src, slot)`` starts copying rank ``src``'s published shard into
     receive slot ``slot`` (0 or 1) and returns a token; ``ready(token)`` waits
     for that copy and returns the slot's tensor; ``finish`` ends the call.
@@ -194,9 +195,14 @@ class CudaIpcExchange(KVExchange):
     while any rank still reads its buffer -- a rank can free its memory or exit
     once its stream is synchronised.
 
-    Ordering inside a rank: a pull into a slot waits for the kernel that last
-    read the slot (an event on the compute stream); a hop's kernel waits for its
-    pull (an event on the copy stream).
+    The publish copy and its barrier run on a side stream while hop 0's kernel
+    reads the caller's K and V directly, so neither sits on the critical path.
+
+    Ordering inside a rank: the publish waits for the compute stream (K and V
+    written, the previous call's trailing barrier passed); a pull waits for the
+    publish barrier and for the kernel that last read its slot (an event on the
+    compute stream); a hop's kernel waits for its pull (an event on the copy
+    stream); the trailing barrier follows the copy and side streams.
 
     One instance serves one (group, shape, dtype, device); ``get_exchange``
     caches them for the life of the process (``release_ring_buffers`` drops
@@ -237,16 +243,28 @@ class CudaIpcExchange(KVExchange):
             self._peer.append(base.value + int.from_bytes(raw[64:72], "little"))
         self._flag = torch.zeros(1, dtype=torch.int32, device=self.device)
         self._copy = [torch.cuda.Stream(self.device) for _ in range(max(1, copy_streams))]
+        # The publish copy and its barrier run here, beside hop 0's kernel
+        # (which reads the caller's own K and V); high priority, so their
+        # kernels take the first SM slot that frees.
+        self._side = torch.cuda.Stream(self.device, priority=-1)
+        self._published = None
 
     def _barrier(self):
         import torch.distributed as dist
         dist.all_reduce(self._flag, group=self.group)   # stream-ordered on the current stream
 
     def publish(self, k, v):
-        self._pub[0].copy_(k)
-        self._pub[1].copy_(v)
-        self._barrier()                                 # every rank has published
-        return self._pub
+        cur = torch.cuda.current_stream(self.device)
+        self._side.wait_stream(cur)                     # k, v written; the last call's trailing barrier passed
+        with torch.cuda.stream(self._side):
+            self._pub[0].copy_(k)
+            self._pub[1].copy_(v)
+            self._barrier()                             # every rank has published
+        self._published = torch.cuda.Event()
+        self._published.record(self._side)
+        k.record_stream(self._side)
+        v.record_stream(self._side)
+        return (k, v)                                   # hop 0 reads the caller's tensors meanwhile
 
     def pull(self, src, slot):
         lib = _lib.load()
@@ -264,6 +282,7 @@ class CudaIpcExchange(KVExchange):
             if size <= 0:
                 break
             s.wait_event(released)
+            s.wait_event(self._published)
             _lib.check(lib.afa_ring_pull(dst0 + lo, src0 + lo, size, s.cuda_stream), "afa_ring_pull")
             ev = torch.cuda.Event()
             ev.record(s)
@@ -281,6 +300,7 @@ class CudaIpcExchange(KVExchange):
         cur = torch.cuda.current_stream(self.device)
         for s in self._copy:
             cur.wait_stream(s)
+        cur.wait_stream(self._side)
         self._barrier()                                 # every rank is done reading every buffer
 
     def close(self) -> None:

@@ -360,7 +360,10 @@ class PhaseTimer:
 
 
 class TimedExchange:
-    """The ring's exchange with its publish and close phases timed."""
+    """The ring's exchange with its publish and close phases timed on the
+    compute stream (the publish copy and its barrier run on the exchange's side
+    stream beside hop 0, so the publish phase shows only what the compute
+    stream itself waits for)."""
 
     def __init__(self, ex, phases):
         self.ex, self.phases, self.rank = ex, phases, ex.rank
