@@ -49,7 +49,7 @@ struct BwdCfg {
   static constexpr int NST = 2;                        // stages of the streamed tile pair
   static constexpr int FIX_OFF = 0;                    // the CTA's two fixed tiles
   static constexpr int ST_OFF = 2 * TILE_BYTES;
-  static constexpr int VEC_OFF = ST_OFF + NST * 2 * TILE_BYTES;  // per grad warp: 32 x (1/d, E) floats
+  static constexpr int VEC_OFF = ST_OFF + NST * 2 * TILE_BYTES;  // per grad warp: 32 x (1/d, -8 scale E) floats
   static constexpr int BAR_OFF = VEC_OFF + 16 * 64 * 4;
   static constexpr int NBAR = 1 + 2 * NST + 6;  // fix_full, st_full[], st_empty[], s_full, x_read, g_full[2], o_full, drain
   static constexpr int SMEM_BYTES = BAR_OFF + NBAR * 8 + 16 + 1024;
@@ -266,8 +266,10 @@ __device__ __forceinline__ void issue(uint8_t* smem, const Bars& b, uint32_t tme
 }
 
 // One 32-column chunk: scores x (raw S or S^T accumulator words), score
-// gradients y (dP or dP^T); per-column (dK/dV kernel) or per-row (dQ kernel)
-// 1/d_total and E. Writes packed bf16 W and dS. Element pairs go through the
+// gradients y (dP or dP^T); per-column (dK/dV kernel: vc[c/2] = (1/d_total of
+// columns c, c+1, then -8 scale E of the same two)) or per-row (dQ kernel:
+// inv_r, ne8_r) factors. ds = 8 scale r w (y - E) is formed as
+// (r w) * fma(y, 8 scale, -8 scale E). Writes packed bf16 W and dS. Element pairs go through the
 // packed fp32x2 instructions (FFMA2 / FMUL2), which halve the issue slots of
 // the map; the one MUFU op per element is the rsqrt. EXACT: the reference's
 // branch form of rho (octic_exact2), for chunks that touch a query row whose
@@ -275,9 +277,9 @@ __device__ __forceinline__ void issue(uint8_t* smem, const Bars& b, uint32_t tme
 // the single-MUFU form cancels.
 template <bool MASK, bool PER_COL, bool EXACT>
 __device__ __forceinline__ void grad_chunk(const uint32_t (&x)[32], const uint32_t (&y)[32], uint32_t (&wp)[16],
-                                           uint32_t (&dp)[16], float scale, const float* inv_c, const float* e_c,
-                                           float inv_r, float e_r, int vis_lim, bool vis_row, int causal,
-                                           int row_pos, int col_pos0, bool row_is_key) {
+                                           uint32_t (&dp)[16], float scale, const float4* vc, float inv_r,
+                                           float ne8_r, int vis_lim, bool vis_row, int causal, int row_pos,
+                                           int col_pos0, bool row_is_key) {
   const float2 sc = make_float2(scale, scale);
   const float2 c8 = make_float2(8.0f * scale, 8.0f * scale);
   const float2 one = make_float2(1.0f, 1.0f);
@@ -295,11 +297,11 @@ __device__ __forceinline__ void grad_chunk(const uint32_t (&x)[32], const uint32
       const float2 p4 = __fmul2_rn(p2, p2);
       p8 = __fmul2_rn(p4, p4);
     }
-    const float2 inv = PER_COL ? make_float2(inv_c[c], inv_c[c + 1]) : make_float2(inv_r, inv_r);
-    const float2 ne = PER_COL ? make_float2(-e_c[c], -e_c[c + 1]) : make_float2(-e_r, -e_r);
-    float2 w = __fmul2_rn(p8, inv);
-    const float2 t = __fadd2_rn(make_float2(__uint_as_float(y[c]), __uint_as_float(y[c + 1])), ne);
-    float2 ds = __fmul2_rn(__fmul2_rn(r, w), __fmul2_rn(t, c8));
+    const float4 cv = PER_COL ? vc[c >> 1] : make_float4(inv_r, inv_r, ne8_r, ne8_r);
+    float2 w = __fmul2_rn(p8, make_float2(cv.x, cv.y));
+    const float2 t8 = __ffma2_rn(make_float2(__uint_as_float(y[c]), __uint_as_float(y[c + 1])), c8,
+                                 make_float2(cv.z, cv.w));
+    float2 ds = __fmul2_rn(__fmul2_rn(r, w), t8);
     if (MASK) {
       // row_is_key: the row is a key, the columns queries; otherwise the reverse.
       const int col = col_pos0 + c;
@@ -353,15 +355,16 @@ __global__ void __launch_bounds__(576, 1)
       const int q0 = 128 * (i_first + it);
       const int qc0 = q0 + 32 * g;
       bool tail;
-      {  // 1/d_total and E of this warp's 32 query columns
+      {  // 1/d_total and -8 scale E of this warp's 32 query columns, as float4s of two columns each
         const int qi = qc0 + lane;
         const bool in = qi < A.L;
         const float dt = in ? A.dtot[rbase + qi] : 1.0f;
-        vec[lane] = in ? 1.0f / dt : 0.0f;
-        vec[32 + lane] = in ? A.e[rbase + qi] : 0.0f;
+        vec[(lane >> 1) * 4 + (lane & 1)] = in ? 1.0f / dt : 0.0f;
+        vec[(lane >> 1) * 4 + 2 + (lane & 1)] = in ? -8.0f * A.scale * A.e[rbase + qi] : 0.0f;
         tail = __any_sync(0xffffffffu, in && tail_row(A, dt));
         __syncwarp();
       }
+      const float4* vc = reinterpret_cast<const float4*>(vec);
       const uint32_t yb = T::y(DBY ? (it & 1) : 0) + lane_off + 32 * g;
       ok = mbar_wait(b.s_full, it & 1, A.status, kDevTimeoutSoftmax);
       ok = __all_sync(0xffffffffu, ok);
@@ -379,13 +382,13 @@ __global__ void __launch_bounds__(576, 1)
       // Columns past L read 1/d = 0, which zeroes W and dS; the mask covers
       // invisible keys and causal order.
       if (tail)
-        grad_chunk<true, true, true>(x, y, wp, dp, A.scale, vec, vec + 32, 0.f, 0.f, A.valid, key < A.L, A.causal,
-                                     key, qc0, true);
+        grad_chunk<true, true, true>(x, y, wp, dp, A.scale, vc, 0.f, 0.f, A.valid, key < A.L, A.causal, key, qc0,
+                                     true);
       else if (need_mask)
-        grad_chunk<true, true, false>(x, y, wp, dp, A.scale, vec, vec + 32, 0.f, 0.f, A.valid, key < A.L, A.causal,
-                                      key, qc0, true);
+        grad_chunk<true, true, false>(x, y, wp, dp, A.scale, vc, 0.f, 0.f, A.valid, key < A.L, A.causal, key, qc0,
+                                      true);
       else
-        grad_chunk<false, true, false>(x, y, wp, dp, A.scale, vec, vec + 32, 0.f, 0.f, 0, true, 0, 0, 0, true);
+        grad_chunk<false, true, false>(x, y, wp, dp, A.scale, vc, 0.f, 0.f, 0, true, 0, 0, 0, true);
       tmem_st16(tmem + yb, dp);       // dS^T over the chunk's first 16 columns
       tmem_st16(tmem + yb + 16, wp);  // W^T over its last 16
       tmem_st_wait();
@@ -475,7 +478,7 @@ __global__ void __launch_bounds__(576, 1)
     const bool in = qry < A.L;
     const float dt = in ? A.dtot[rbase + qry] : 1.0f;
     const float inv = in ? 1.0f / dt : 0.0f;
-    const float ev = in ? A.e[rbase + qry] : 0.0f;
+    const float ne8 = in ? -8.0f * A.scale * A.e[rbase + qry] : 0.0f;
     const bool tail = __any_sync(0xffffffffu, in && tail_row(A, dt));
     bool ok = true;
     for (int it = 0; ok && it < niter; ++it) {
@@ -495,13 +498,13 @@ __global__ void __launch_bounds__(576, 1)
       if (lane == 0) mbar_arrive(b.x_read);
       const bool need_mask = 128 * it + 127 >= A.valid || (A.causal && 128 * it + 127 > q0);
       if (tail)
-        grad_chunk<true, false, true>(x, y, wp, dp, A.scale, nullptr, nullptr, inv, ev, A.valid, in, A.causal, qry,
-                                      kc0, false);
+        grad_chunk<true, false, true>(x, y, wp, dp, A.scale, nullptr, inv, ne8, A.valid, in, A.causal, qry, kc0,
+                                      false);
       else if (need_mask)
-        grad_chunk<true, false, false>(x, y, wp, dp, A.scale, nullptr, nullptr, inv, ev, A.valid, in, A.causal, qry,
-                                       kc0, false);
+        grad_chunk<true, false, false>(x, y, wp, dp, A.scale, nullptr, inv, ne8, A.valid, in, A.causal, qry, kc0,
+                                       false);
       else
-        grad_chunk<false, false, false>(x, y, wp, dp, A.scale, nullptr, nullptr, inv, ev, 0, true, 0, 0, 0, false);
+        grad_chunk<false, false, false>(x, y, wp, dp, A.scale, nullptr, inv, ne8, 0, true, 0, 0, 0, false);
       // dS over the chunk's first 16 dP columns: the A operand of dQ += dS K.
       tmem_st16(tmem + yb, dp);
       tmem_st_wait();
