@@ -3,9 +3,9 @@
 // Same math as afa_bwd.cu (tiled_afa_backward, src/kernels/pallas_afa.py:
 // 409-522): w = rho(s)^8 / d_total, ds = 8 scale r w (g_out.v - E),
 // dq = ds k, dk = ds^T q, dv = w^T g_out, with w and ds rounded to bf16 before
-// the products (:440-448) and fp32 accumulation. rho uses the single-MUFU form
-// of the forward kernel (rho = (1+s^2) rsqrt(1+s^2) + s), whose rsqrt is also
-// the r of the score derivative.
+// the products (:440-448) and fp32 accumulation. rho uses a single-MUFU form,
+// rho = (1+s^2) rsqrt(1+s^2) + s, whose rsqrt is also the r of the score
+// derivative.
 //
 // Two kernels, each with the forward's warp roles (576 threads: 16 "grad"
 // warps, 1 TMA warp, 1 MMA-issue warp) and one CTA per SM:

@@ -56,14 +56,25 @@ __device__ __forceinline__ double octic_ref(double s) {
   return k4 * k4;
 }
 
-// Tensor-core fast form: rho = (1 + s^2) * rsqrt(1 + s^2) + s in one FMA for
-// both signs -- the reference's positive branch (pallas_afa.py:46) applied to
-// every s -- with one MUFU op per score, on a pair of scores with the sm_100
-// packed FP32 instructions (FFMA2 / FMUL2). The tensor-core kernels are bound
-// by MUFU/issue throughput, and the conjugate negative branch costs a second
-// MUFU op (a reciprocal) per score, which measured 30-45% slower.
-// Error: rsqrt.approx has relative error |d| <= 2^-22.9 and 1 + s^2 is rounded
-// once (2^-24), so rho(s) for s >= 0 is within ~2^-22; for s < 0 the sum
+// Hardware square root (MUFU), flush-to-zero form.
+__device__ __forceinline__ float sqrt_approx(float x) {
+  float y;
+  asm("sqrt.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// Tensor-core fast form: rho = s + sqrt(1 + s^2) for both signs -- the
+// reference's positive branch (pallas_afa.py:46, which forms the square root
+// as (1 + s^2) * rsqrt(1 + s^2)) applied to every s -- with one MUFU op per
+// score, on a pair of scores with the sm_100 packed FP32 instructions
+// (FFMA2 / FADD2 / FMUL2). The tensor-core kernels are bound by MUFU/issue
+// throughput, and the conjugate negative branch costs a second MUFU op (a
+// reciprocal) per score, which measured 30-45% slower. sqrt.approx then an
+// add mapped 2.5% faster than rsqrt.approx then an FMA (+4% on an L = 4096
+// prefill).
+// Error: sqrt.approx measured relative error |d| <= 2^-23.3 (rsqrt.approx
+// 2^-22.9) over 2^24 inputs in [1, 2^60], and 1 + s^2 is rounded once
+// (2^-24), so rho(s) for s >= 0 is within ~2^-22.5; for s < 0 the sum
 // cancels (rho ~ 1/(2|s|) against terms of size |s|) and the relative error of
 // rho grows to ~ 2 s^2 (|d| + 2^-25), i.e. rho^8 to ~ 2.5e-6 s^2: 6.4e-4 at
 // s = -16, 1% at s = -64, 16% at s = -256. The kernels therefore use this form
@@ -71,8 +82,7 @@ __device__ __forceinline__ double octic_ref(double s) {
 // kTailRowSum) and octic_exact2 elsewhere.
 __device__ __forceinline__ float2 octic_fast2(float2 s) {
   const float2 rad = __ffma2_rn(s, s, make_float2(1.0f, 1.0f));
-  const float2 r = make_float2(rsqrt_approx(rad.x), rsqrt_approx(rad.y));
-  const float2 rho = __ffma2_rn(rad, r, s);
+  const float2 rho = __fadd2_rn(make_float2(sqrt_approx(rad.x), sqrt_approx(rad.y)), s);
   const float2 k2 = __fmul2_rn(rho, rho);
   const float2 k4 = __fmul2_rn(k2, k2);
   return __fmul2_rn(k4, k4);
