@@ -269,7 +269,9 @@ __device__ __forceinline__ void issue(uint8_t* smem, const Bars& b, uint32_t tme
 // gradients y (dP or dP^T); per-column (dK/dV kernel: vc[c/2] = (1/d_total of
 // columns c, c+1, then -8 scale E of the same two)) or per-row (dQ kernel:
 // inv_r, ne8_r) factors. ds = 8 scale r w (y - E) is formed as
-// (r w) * fma(y, 8 scale, -8 scale E). Writes packed bf16 W and dS. Element pairs go through the
+// (r w) * fma(y, 8 scale, -8 scale E); w = p8 / d_total <= 1 keeps every
+// product in range. Writes packed bf16 dS, and W per column (the dQ kernel
+// needs no W). Element pairs go through the
 // packed fp32x2 instructions (FFMA2 / FMUL2), which halve the issue slots of
 // the map; the one MUFU op per element is the rsqrt. EXACT: the reference's
 // branch form of rho (octic_exact2), for chunks that touch a query row whose
@@ -282,6 +284,7 @@ __device__ __forceinline__ void grad_chunk(const uint32_t (&x)[32], const uint32
                                            int col_pos0, bool row_is_key) {
   const float2 sc = make_float2(scale, scale);
   const float2 c8 = make_float2(8.0f * scale, 8.0f * scale);
+  const float2 invr = make_float2(inv_r, inv_r), ne8r = make_float2(ne8_r, ne8_r);
   const float2 one = make_float2(1.0f, 1.0f);
 #pragma unroll
   for (int c = 0; c < 32; c += 2) {
@@ -297,11 +300,15 @@ __device__ __forceinline__ void grad_chunk(const uint32_t (&x)[32], const uint32
       const float2 p4 = __fmul2_rn(p2, p2);
       p8 = __fmul2_rn(p4, p4);
     }
-    const float4 cv = PER_COL ? vc[c >> 1] : make_float4(inv_r, inv_r, ne8_r, ne8_r);
-    float2 w = __fmul2_rn(p8, make_float2(cv.x, cv.y));
-    const float2 t8 = __ffma2_rn(make_float2(__uint_as_float(y[c]), __uint_as_float(y[c + 1])), c8,
-                                 make_float2(cv.z, cv.w));
-    float2 ds = __fmul2_rn(__fmul2_rn(r, w), t8);
+    const float2 yv = make_float2(__uint_as_float(y[c]), __uint_as_float(y[c + 1]));
+    float2 w = make_float2(0.f, 0.f), ds;
+    if constexpr (PER_COL) {
+      const float4 cv = vc[c >> 1];
+      w = __fmul2_rn(p8, make_float2(cv.x, cv.y));
+      ds = __fmul2_rn(__fmul2_rn(r, w), __ffma2_rn(yv, c8, make_float2(cv.z, cv.w)));
+    } else {
+      ds = __fmul2_rn(__fmul2_rn(r, __fmul2_rn(p8, invr)), __ffma2_rn(yv, c8, ne8r));
+    }
     if (MASK) {
       // row_is_key: the row is a key, the columns queries; otherwise the reverse.
       const int col = col_pos0 + c;
@@ -314,7 +321,7 @@ __device__ __forceinline__ void grad_chunk(const uint32_t (&x)[32], const uint32
       ds.x = v0 ? ds.x : 0.0f;
       ds.y = v1 ? ds.y : 0.0f;
     }
-    wp[c >> 1] = pack_bf16x2(w.x, w.y);
+    if constexpr (PER_COL) wp[c >> 1] = pack_bf16x2(w.x, w.y);
     dp[c >> 1] = pack_bf16x2(ds.x, ds.y);
   }
 }
