@@ -38,6 +38,7 @@ SIGNATURES = {
     "afa_ring_open": (_c_int, [_c_void_p, ctypes.POINTER(_c_void_p)]),
     "afa_ring_close": (_c_int, [_c_void_p]),
     "afa_ring_pull": (_c_int, [_c_void_p, _c_void_p, _c_size, _c_void_p]),
+    "afa_ring_pull2d": (_c_int, [_c_void_p, _c_size, _c_void_p, _c_size, _c_size, _c_size, _c_void_p]),
     "afa_decode": (_c_int, [_c_void_p] * 5 + [_c_int] * 5 + [_c_float, _c_void_p, _c_int, _c_void_p, _c_size,
                                                              _c_void_p]),
     "afa_decode_workspace_bytes": (_c_size, [_c_int] * 4),

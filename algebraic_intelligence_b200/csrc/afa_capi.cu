@@ -170,14 +170,20 @@ int afa_fwd_hop(const void* q, const void* k, const void* v, void* o_acc, void* 
     if (causal && P.nk == 2 && P.k[0].pos0 + P.k[0].len - 1 > P.q.pos0)
       return fail(AFA_ERR_INVALID,
                   "problem %d: with causal masking the first key segment must be visible to every query row", i);
-    for (int j = 0; j < i; ++j) {
-      const afa::Segment& a = Lc.prob[j].q;
-      if (a.row0 < P.q.row0 + P.q.len && P.q.row0 < a.row0 + a.len)
-        return fail(AFA_ERR_INVALID, "problems %d and %d write overlapping query rows", j, i);
-    }
   }
   static const int kModeMap[4] = {afa::kStoreRaw, afa::kAccumRaw, afa::kAccumFinal, afa::kFinal};
   Lc.mode = kModeMap[mode];
+  // Query rows shared by two problems only add up where the launch adds its
+  // pieces with reductions (merged accumulate hops on the tensor cores).
+  if (!afa::tc_accum_reduces(Lc, dtype)) {
+    for (int i = 0; i < nproblems; ++i)
+      for (int j = 0; j < i; ++j) {
+        const afa::Segment& a = Lc.prob[j].q;
+        const afa::Segment& b = Lc.prob[i].q;
+        if (a.row0 < b.row0 + b.len && b.row0 < a.row0 + a.len)
+          return fail(AFA_ERR_INVALID, "problems %d and %d write overlapping query rows", j, i);
+      }
+  }
   Lc.q = q;
   Lc.k = k;
   Lc.v = v;

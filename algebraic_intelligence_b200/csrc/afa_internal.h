@@ -59,6 +59,10 @@ inline int assign_ctas(Launch& L, int rows_per_cta) {
 // Each returns cudaSuccess or the launch error; `detail` receives a short
 // message on failure.
 bool tc_fwd_supported(int dtype, int d);
+// True when an accumulate launch of these problems runs the persistent
+// tensor-core kernel, whose pieces add into the accumulators with reductions,
+// so two problems may share query rows (their partial sums add).
+bool tc_accum_reduces(const Launch& L, int dtype);
 cudaError_t launch_tc_fwd(Launch L, int dtype, cudaStream_t stream, const char** detail);
 
 cudaError_t launch_simt_fwd(Launch L, int dtype, cudaStream_t stream, const char** detail);

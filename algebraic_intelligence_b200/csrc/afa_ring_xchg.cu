@@ -96,3 +96,15 @@ extern "C" int afa_ring_pull(void* dst, const void* src, size_t bytes, void* str
   if (e != cudaSuccess) return cuda_fail("afa_ring_pull: cudaMemcpyAsync", e);
   return AFA_OK;
 }
+
+extern "C" int afa_ring_pull2d(void* dst, size_t dst_pitch, const void* src, size_t src_pitch, size_t row_bytes,
+                               size_t rows, void* stream) {
+  if (row_bytes == 0 || rows == 0) return AFA_OK;
+  if (!dst || !src) return afa::set_last_error(AFA_ERR_INVALID, "afa_ring_pull2d: null pointer");
+  if (dst_pitch < row_bytes || src_pitch < row_bytes)
+    return afa::set_last_error(AFA_ERR_INVALID, "afa_ring_pull2d: a pitch is shorter than a row");
+  cudaError_t e = cudaMemcpy2DAsync(dst, dst_pitch, src, src_pitch, row_bytes, rows, cudaMemcpyDefault,
+                                    static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail("afa_ring_pull2d: cudaMemcpy2DAsync", e);
+  return AFA_OK;
+}

@@ -1037,6 +1037,12 @@ cudaError_t launch_hd(const Launch& L, cudaStream_t stream, const char** detail)
 
 bool tc_fwd_supported(int dtype, int d) { return dtype == kBF16 && (d == 64 || d == 128); }
 
+bool tc_accum_reduces(const Launch& L, int dtype) {
+  if (!tc_fwd_supported(dtype, L.d) || L.mode != kAccumRaw) return false;
+  Launch LL = L;
+  return assign_ctas(LL, 256) <= kMaxSkItems;  // the condition launch_hd takes the persistent kernel on
+}
+
 cudaError_t launch_tc_fwd(Launch L, int dtype, cudaStream_t stream, const char** detail) {
   if (!tc_fwd_supported(dtype, L.d)) {
     *detail = "tensor-core path needs bf16 and head_dim 64 or 128";

@@ -17,7 +17,10 @@ B200 form:
   send/receive pair per hop;
 * a hop is one launch of the grouped forward kernel (``afa_fwd_hop``): the
   first hop stores the accumulators, middle hops add, and the last hop adds and
-  divides in its epilogue -- no separate normalisation pass;
+  divides. On the tensor cores two consecutive middle hops share one launch
+  (``launch_groups``): their shards are pulled side by side into one receive
+  buffer, so the fixed cost of a launch (prologue, split tail, drain) is paid
+  once for both;
 * ``layout="zigzag"`` (default for causal work) cuts the sequence into 2P
   chunks and gives rank r chunks r and 2P-1-r, which balances causal work;
   fully masked (query, key) chunk pairs are skipped on the host and partially
@@ -35,7 +38,8 @@ import torch
 from . import _lib
 
 __all__ = ["distributed_ring_afa", "shard_sequence", "unshard_sequence", "ring_plan", "RingHop", "local_segments",
-           "ring_loop", "KVExchange", "ListExchange", "CudaIpcExchange", "get_exchange", "release_ring_buffers"]
+           "merge_hops", "launch_groups", "ring_loop", "KVExchange", "ListExchange", "CudaIpcExchange", "get_exchange",
+           "release_ring_buffers"]
 
 Segment = Tuple[int, int, int]  # (row0 in the local shard, length, global position of row0)
 
@@ -133,6 +137,52 @@ def ring_plan(rank: int, world: int, seq_len: int, causal: bool, layout: str) ->
     return hops
 
 
+# Query pairs (256 rows) per (batch, head) that the persistent accumulate
+# kernel plans (kMaxSkItems in csrc/afa_tc_shared.cuh); a larger launch runs
+# the one-CTA-per-pair kernel, whose accumulate epilogue must not see one query
+# row in two problems.
+_SK_MAX_PAIRS = 1024
+_MAX_PROBLEMS = 4
+
+
+def merge_hops(group: Sequence[RingHop], shard_len: int) -> RingHop:
+    """One launch for consecutive accumulate hops whose shards sit side by side
+    in one receive buffer: hop j's keys at rows [j*shard_len, (j+1)*shard_len)
+    of every (batch, head) block. Their partial sums only add, so the launch
+    computes the same as the hops one after the other."""
+    problems = []
+    for j, h in enumerate(group):
+        for qr, ql, qp, keys in h.problems:
+            problems.append((qr, ql, qp, [(kr + j * shard_len, kl, kp) for kr, kl, kp in keys]))
+    return RingHop(src=group[0].src, mode=group[0].mode, problems=problems)
+
+
+def launch_groups(hops: Sequence[RingHop], shard_len: int, max_hops: int = 2):
+    """The launches of one ring call: ``[(member hops, launched hop), ...]``.
+    Wholly masked hops are left out (they pull and compute nothing). The
+    first hop (STORE) and the last (FINALIZE) launch alone; consecutive
+    accumulate hops are merged in pairs when ``max_hops`` allows it and the
+    merged launch fits the persistent kernel (at most four problems and
+    _SK_MAX_PAIRS query pairs per head), halving the per-launch prologue,
+    split tail and drain of those hops."""
+    live = [h for h in hops if h.problems]
+    groups = []
+    i = 0
+    while i < len(live):
+        h = live[i]
+        if (max_hops > 1 and h.mode == _lib.AFA_HOP_ACCUMULATE and i + 1 < len(live)
+                and live[i + 1].mode == _lib.AFA_HOP_ACCUMULATE):
+            m = merge_hops(live[i:i + 2], shard_len)
+            pairs = sum(-(-ql // 256) for _, ql, _, _ in m.problems)
+            if len(m.problems) <= _MAX_PROBLEMS and pairs <= _SK_MAX_PAIRS:
+                groups.append((list(live[i:i + 2]), m))
+                i += 2
+                continue
+        groups.append(([h], h))
+        i += 1
+    return groups
+
+
 class KVExchange:
     """How the hops of one ring call obtain their K/V shards.
 
@@ -142,10 +192,14 @@ class KVExchange:
     ``pull(src, slot)`` starts copying rank ``src``'s published shard into
     receive slot ``slot`` (0 or 1) and returns a token; ``ready(token)`` waits
     for that copy and returns the slot's tensor; ``finish`` ends the call.
-    Subclasses are the transports.
+    Transports with ``max_group`` > 1 also have ``pull_group(srcs, slot)``: the
+    shards of ``srcs`` side by side along the sequence (rows
+    [j*S, (j+1)*S) of every (batch, head) block hold srcs[j]'s), for one launch
+    of merged hops (``launch_groups``). Subclasses are the transports.
     """
 
     rank = 0
+    max_group = 1
 
     def publish(self, k: torch.Tensor, v: torch.Tensor) -> torch.Tensor:
         raise NotImplementedError
@@ -164,10 +218,13 @@ class ListExchange(KVExchange):
     """Every rank's shard already lives in this process (a ring emulated in one
     process, rank by rank): ``shards[r]`` is rank r's (2, B, H, S, D) K/V."""
 
+    max_group = 2
+
     def __init__(self, rank: int, shards: Sequence[torch.Tensor]):
         self.rank = rank
         self.shards = list(shards)
         self.recv = [torch.empty_like(self.shards[rank]) for _ in range(2)]
+        self.recv_n = {}
 
     def publish(self, k, v):
         return self.shards[self.rank]
@@ -176,7 +233,21 @@ class ListExchange(KVExchange):
         self.recv[slot].copy_(self.shards[src])
         return slot
 
+    def pull_group(self, srcs, slot):
+        n = len(srcs)
+        mine = self.shards[self.rank]
+        s = mine.shape[3]
+        if n not in self.recv_n:
+            shape = mine.shape[:3] + (n * s,) + mine.shape[4:]
+            self.recv_n[n] = [torch.empty(shape, dtype=mine.dtype, device=mine.device) for _ in range(2)]
+        buf = self.recv_n[n][slot]
+        for j, src in enumerate(srcs):
+            buf[:, :, :, j * s:(j + 1) * s].copy_(self.shards[src])
+        return ("group", n, slot)
+
     def ready(self, token):
+        if isinstance(token, tuple) and token[0] == "group":
+            return self.recv_n[token[1]][token[2]]
         return self.recv[token]
 
 
@@ -241,6 +312,8 @@ class CudaIpcExchange(KVExchange):
             _lib.check(lib.afa_ring_open(raw[:64], ctypes.byref(base)), "afa_ring_open")
             self._bases.append(base.value)
             self._peer.append(base.value + int.from_bytes(raw[64:72], "little"))
+        self._shape = tuple(shape)
+        self._recv_n = {}  # receive slots for merged hops, by hop count: [slot] -> (2, B, H, n*S, D)
         self._flag = torch.zeros(1, dtype=torch.int32, device=self.device)
         self._copy = [torch.cuda.Stream(self.device) for _ in range(max(1, copy_streams))]
         # The publish copy and its barrier run here, beside hop 0's kernel
@@ -289,12 +362,47 @@ class CudaIpcExchange(KVExchange):
             done.append(ev)
         return slot, done
 
+    max_group = 2
+
+    def pull_group(self, srcs, slot):
+        """The shards of ``srcs`` side by side in one receive slot: each K and V
+        goes into its rows of every (batch, head) block with one strided copy
+        (``afa_ring_pull2d``) on the copy stream."""
+        lib = _lib.load()
+        n = len(srcs)
+        if n not in self._recv_n:
+            b, h, s, d = self._shape
+            self._recv_n[n] = torch.empty((2, 2, b, h, n * s, d), dtype=self._pub.dtype, device=self.device)
+        buf = self._recv_n[n][slot]
+        cur = torch.cuda.current_stream(self.device)
+        released = torch.cuda.Event()
+        released.record(cur)
+        cs = self._copy[0]
+        cs.wait_event(released)
+        cs.wait_event(self._published)
+        b, h, s, d = self._shape
+        row = s * d * self._pub.element_size()   # one (batch, head) block of one shard's K (or V)
+        for j, src in enumerate(srcs):
+            for kv in (0, 1):
+                dst = buf[kv].data_ptr() + j * row
+                src_ptr = self._peer[src] + kv * (self.nbytes // 2)
+                _lib.check(lib.afa_ring_pull2d(dst, n * row, src_ptr, row, row, b * h, cs.cuda_stream),
+                           "afa_ring_pull2d")
+        ev = torch.cuda.Event()
+        ev.record(cs)
+        return ("group", n, slot, [ev])
+
     def ready(self, token):
-        slot, done = token
+        if token[0] == "group":
+            _, n, slot, done = token
+            buf = self._recv_n[n][slot]
+        else:
+            slot, done = token
+            buf = self._recv[slot]
         cur = torch.cuda.current_stream(self.device)
         for ev in done:
             cur.wait_event(ev)
-        return self._recv[slot]
+        return buf
 
     def finish(self):
         cur = torch.cuda.current_stream(self.device)
@@ -345,14 +453,18 @@ def release_ring_buffers() -> None:
 
 
 def ring_loop(k: torch.Tensor, v: torch.Tensor, hops: List[RingHop], compute: Callable,
-              exchange: Optional[KVExchange]) -> None:
+              exchange: Optional[KVExchange], merge: Optional[bool] = None) -> None:
     """Drive the hops of one ring call.
 
-    ``compute(hop, k, v)`` runs one hop on that hop's K/V. Hop 0 reads this
-    rank's own shard; hop i pulls the shard of rank ``hop.src`` from its owner,
-    the pull for hop i+1 starting before hop i's compute so the two overlap
-    (two receive slots). Hops whose problems are empty (wholly masked) pull
-    nothing. With one rank (``exchange`` None) the only hop reads k and v.
+    ``compute(hop, k, v)`` runs one launch (``launch_groups``: one hop, or two
+    merged accumulate hops when the exchange can pull two shards into one
+    buffer) on that launch's K/V. The first launch reads this rank's own shard;
+    later ones pull the shards of their hops' ``src`` ranks from their owners,
+    the pull for launch g+1 starting before launch g's compute so the two
+    overlap (two receive slots). Wholly masked hops pull and compute nothing.
+    With one rank (``exchange`` None) the only hop reads k and v. ``merge``
+    None merges where the launches run on the tensor cores (bf16, head_dim 64
+    or 128); True or False forces it (tests of the protocol use small shapes).
     """
     if exchange is None:
         for hop in hops:
@@ -362,18 +474,26 @@ def ring_loop(k: torch.Tensor, v: torch.Tensor, hops: List[RingHop], compute: Ca
     local = exchange.publish(k, v)
     if hops and hops[0].src != exchange.rank:
         raise ValueError("the first hop of a ring plan must read the rank's own shard")
+    # Only the tensor cores' persistent accumulate kernel adds one query row's
+    # partial sums from two problems of a launch (fire-and-forget reductions);
+    # the CUDA-core kernels read-modify-write them, so their hops stay apart.
+    if merge is None:
+        merge = k.dtype == torch.bfloat16 and k.shape[3] in (64, 128)
+    groups = launch_groups(hops, k.shape[2], getattr(exchange, "max_group", 1) if merge else 1)
 
-    def start(i):
-        if 0 < i < len(hops) and hops[i].problems:
-            return exchange.pull(hops[i].src, i % 2)
+    def start(g):
+        if 0 < g < len(groups):
+            members = groups[g][0]
+            if len(members) == 1:
+                return exchange.pull(members[0].src, g % 2)
+            return exchange.pull_group([h.src for h in members], g % 2)
         return None
 
     pending = None
-    for i, hop in enumerate(hops):
-        kv = local if i == 0 else (exchange.ready(pending) if pending is not None else None)
-        pending = start(i + 1)
-        if hop.problems:
-            compute(hop, kv[0], kv[1])
+    for g, (_members, hop) in enumerate(groups):
+        kv = local if g == 0 else exchange.ready(pending)
+        pending = start(g + 1)
+        compute(hop, kv[0], kv[1])
     exchange.finish()
 
 

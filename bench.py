@@ -263,13 +263,18 @@ def ring_inputs(rank, world, seed):
 def run_ring(args, rank, world, peaks, traffic):
     import torch
     import algebraic_intelligence_b200 as afa
+    from algebraic_intelligence_b200 import _lib
     from algebraic_intelligence_b200.afa import hop_forward
     from algebraic_intelligence_b200.ring import ring_plan
 
     sets = [ring_inputs(rank, world, seed) for seed in (0, 1)]  # 2 sets: > L2 between steps
     flops = causal_flops(**RING)
     hops = ring_plan(rank, world, RING["L"], True, "zigzag")
-    launches_per_step = sum(1 for h in hops if h.problems) if world > 1 else 1
+    if world > 1:
+        from algebraic_intelligence_b200.ring import launch_groups
+        launches_per_step = len(launch_groups(hops, RING["L"] // world))
+    else:
+        launches_per_step = 1
 
     if world == 1:
         def step(i, kt):
@@ -287,7 +292,6 @@ def run_ring(args, rank, world, peaks, traffic):
         exchange = get_exchange(q0.shape, q0.dtype, q0.device)   # the one distributed_ring_afa uses
         phases = PhaseTimer()
         timed_exchange = TimedExchange(exchange, phases)
-        live = [i for i, hp in enumerate(hops) if hp.problems]
 
         def step(i, kt):
             q, k, v = sets[i % 2]
@@ -298,8 +302,8 @@ def run_ring(args, rank, world, peaks, traffic):
                 if kt is None:
                     f()
                     return
-                j = next(n for n, hp in enumerate(hops) if hp is hop)
-                name = "hop0_store" if j == live[0] else ("hop_last_finalize" if j == live[-1] else "hop_accumulate")
+                name = {_lib.AFA_HOP_STORE: "hop0_store", _lib.AFA_HOP_FINALIZE: "hop_last_finalize"}.get(
+                    hop.mode, "hop_accumulate")
                 phases.around(name, lambda: kt.around(f))
 
             ring_loop(k, v, hops, compute, timed_exchange if kt is not None else exchange)
@@ -326,10 +330,11 @@ def run_ring(args, rank, world, peaks, traffic):
     if world > 1:
         # Where a ring step's time goes, max over ranks (ms per step; per launch
         # for the hop kernels): the first hop's STORE kernel, the accumulate
-        # hops' kernels, the last hop (accumulate + divide), the publish (K/V
-        # copy into the IPC buffer + the first barrier) and the close (joining
-        # the copy stream + the second barrier).
+        # launches (two merged hops each where launch_groups pairs them), the
+        # last hop (accumulate + divide), the publish and the close (what the
+        # compute stream waits for of the K/V publish and the two barriers).
         res["hop_breakdown"] = {k: max_over_ranks(v, world) for k, v in phases.summary(args.steps).items()}
+        res["hop_breakdown"]["launches_per_step"] = launches_per_step
     del sets
     return res
 

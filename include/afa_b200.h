@@ -103,8 +103,12 @@ AFA_API int afa_fwd(const void* q, const void* k, const void* v, void* out, void
  *               With causal, key position <= query position decides
  *               visibility (pallas_afa.py:640-646); a segment may be wholly
  *               invisible (no tiles run, the epilogue still does). Query ranges
- *               of different problems must not overlap; with two key segments
- *               and causal, the first must be visible to every query row.
+ *               of different problems must not overlap, except in
+ *               AFA_HOP_ACCUMULATE on the tensor cores (bf16, D 64 or 128,
+ *               at most 1024 query pairs of 256 rows per (b, h)), where the
+ *               partial sums of shared rows add (two ring hops in one launch);
+ *               with two key segments and causal, the first must be visible to
+ *               every query row.
  *   mode        AFA_HOP_STORE      o_acc = O, d_acc = d          (first hop)
  *               AFA_HOP_ACCUMULATE o_acc += O, d_acc += d        (middle hops)
  *               AFA_HOP_FINALIZE   out = (o_acc + O) / (d_acc + d + sink),
@@ -149,12 +153,19 @@ AFA_API int afa_finalize(const void* o_acc, const void* d_acc, void* out, void* 
  *   afa_ring_close   unmaps a base returned by afa_ring_open.
  *   afa_ring_pull    stream-ordered copy of `bytes` from src (a peer mapping
  *                    or local memory) to dst on the copy engines.
+ *   afa_ring_pull2d  the same for `rows` rows of `row_bytes` bytes, src rows
+ *                    `src_pitch` bytes apart and dst rows `dst_pitch` apart:
+ *                    a shard pulled into half of every (batch, head) block of
+ *                    a receive buffer that holds two hops' shards, so one
+ *                    kernel launch computes both hops.
  */
 #define AFA_RING_HANDLE_BYTES 64
 AFA_API int afa_ring_export(const void* ptr, void* handle_out, unsigned long long* offset_out);
 AFA_API int afa_ring_open(const void* handle, void** base_out);
 AFA_API int afa_ring_close(void* base);
 AFA_API int afa_ring_pull(void* dst, const void* src, size_t bytes, void* stream);
+AFA_API int afa_ring_pull2d(void* dst, size_t dst_pitch, const void* src, size_t src_pitch, size_t row_bytes,
+                            size_t rows, void* stream);
 
 /*
  * Backward (tiled_afa_backward, pallas_afa.py:409-522; the VJP of pallas_afa,

@@ -108,6 +108,11 @@ def test_ring_exchange_argument_checks():
     assert lib.afa_ring_pull(None, 1, 16, None) == _lib.AFA_ERR_INVALID
     assert b"afa_ring_pull" in lib.afa_last_error()
     assert lib.afa_ring_pull(None, None, 0, None) == _lib.AFA_OK
+    assert lib.afa_ring_pull2d(None, 64, 1, 32, 16, 2, None) == _lib.AFA_ERR_INVALID
+    assert b"afa_ring_pull2d" in lib.afa_last_error()
+    assert lib.afa_ring_pull2d(1, 8, 1, 32, 16, 2, None) == _lib.AFA_ERR_INVALID
+    assert b"pitch" in lib.afa_last_error()
+    assert lib.afa_ring_pull2d(None, 0, None, 0, 0, 0, None) == _lib.AFA_OK
 
 
 def test_backward_argument_checks():

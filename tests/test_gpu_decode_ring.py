@@ -130,12 +130,12 @@ def test_decode_matches_prefill_row():
 # ---------------------------------------------------------------------------
 # ring, emulated on one GPU
 # ---------------------------------------------------------------------------
-def emulate_ring(q, k, v, world, causal, layout, sink=0.5):
+def emulate_ring(q, k, v, world, causal, layout, sink=0.5, merge=None, with_den=False):
     """Runs ring_plan + ring_loop + the hop kernel for every rank on this GPU."""
     seq = q.shape[2]
     kvs = [torch.stack([shard_sequence(k, r, world, layout), shard_sequence(v, r, world, layout)])
            for r in range(world)]
-    outs = []
+    outs, dens = [], []
     for r in range(world):
         qs = shard_sequence(q, r, world, layout)
         b, h, s, d = qs.shape
@@ -149,8 +149,11 @@ def emulate_ring(q, k, v, world, causal, layout, sink=0.5):
             hop_forward(qs, kk, vv, hop.problems, causal, hop.mode, o_acc=o_acc, d_acc=d_acc, out=out,
                         d_total=den, sink_omega=sink)
 
-        ring_loop(kvs[r][0], kvs[r][1], hops, compute, ListExchange(r, kvs) if world > 1 else None)
+        ring_loop(kvs[r][0], kvs[r][1], hops, compute, ListExchange(r, kvs) if world > 1 else None, merge=merge)
         outs.append(out)
+        dens.append(den)
+    if with_den:
+        return unshard_sequence(outs, layout), unshard_sequence(dens, layout)
     return unshard_sequence(outs, layout)
 
 
@@ -183,6 +186,22 @@ def test_ring_bf16_tensor_core_path(world, causal, layout):
     single = afa.pallas_afa_forward(q, k, v, causal=causal)
     # both sides round to bf16 at the end; fp32 accumulators differ only in order
     assert orc.rel_err(host64(ring), host64(single)) <= 1e-2
+
+
+@pytest.mark.parametrize("world,layout", [(4, "zigzag"), (8, "zigzag"), (8, "contiguous")])
+def test_ring_merged_hops_match_separate_hops(world, layout):
+    """Two accumulate hops in one launch (their shards side by side in one
+    receive buffer) give what the two launches give: the same partial sums in
+    another order, so d_total agrees to fp32 summation order and the bf16
+    outputs to their rounding."""
+    g = torch.Generator(device="cuda").manual_seed(21)
+    q, k, v = (torch.randn((2, 2, 4096, 128), generator=g, device="cuda").to(torch.bfloat16) for _ in range(3))
+    a, da = emulate_ring(q, k, v, world, True, layout, merge=True, with_den=True)
+    b, db = emulate_ring(q, k, v, world, True, layout, merge=False, with_den=True)
+    assert torch.isfinite(a.float()).all()
+    assert orc.rel_err(host64(da), host64(db)) <= 1e-5
+    assert orc.rel_err(host64(a), host64(b)) <= 1e-2
+    assert _lib.device_status(q.device) == 0
 
 
 def test_ring_api_single_process():

@@ -9,7 +9,7 @@ import torch
 
 import algebraic_intelligence_b200 as afa
 from algebraic_intelligence_b200 import _lib
-from algebraic_intelligence_b200.ring import (KVExchange, ListExchange, local_segments, ring_loop, ring_plan,
+from algebraic_intelligence_b200.ring import (KVExchange, ListExchange, launch_groups, local_segments, ring_loop, ring_plan,
                                               shard_sequence, unshard_sequence)
 from oracle import afa_oracle as orc
 
@@ -214,13 +214,15 @@ class _SharedMemoryExchange(KVExchange):
     shared-memory tensors every process maps, the barriers gloo barriers, a
     pull a copy out of the owner's buffer. ``pubs[r]`` is rank r's."""
 
-    def __init__(self, rank, pubs, log):
+    def __init__(self, rank, pubs, log, max_group=1):
         import torch.distributed as dist
         self.dist = dist
         self.rank = rank
         self.pubs = pubs
         self.recv = [torch.empty_like(pubs[rank]) for _ in range(2)]
         self.log = log
+        self.max_group = max_group
+        self.recv_n = {}
 
     def publish(self, k, v):
         buf = self.pubs[self.rank]
@@ -234,7 +236,20 @@ class _SharedMemoryExchange(KVExchange):
         self.recv[slot].copy_(self.pubs[src])
         return slot
 
+    def pull_group(self, srcs, slot):
+        self.log.append(("pull", tuple(srcs), slot))
+        mine = self.pubs[self.rank]
+        s = mine.shape[3]
+        n = len(srcs)
+        if n not in self.recv_n:
+            self.recv_n[n] = [torch.empty(mine.shape[:3] + (n * s,) + mine.shape[4:]) for _ in range(2)]
+        for j, src in enumerate(srcs):
+            self.recv_n[n][slot][:, :, :, j * s:(j + 1) * s].copy_(self.pubs[src])
+        return ("group", n, slot)
+
     def ready(self, token):
+        if isinstance(token, tuple):
+            return self.recv_n[token[1]][token[2]]
         return self.recv[token]
 
     def finish(self):
@@ -242,28 +257,30 @@ class _SharedMemoryExchange(KVExchange):
         self.dist.barrier()
 
 
-def _gloo_worker(rank, world, port, pubs, causal, results):
+def _gloo_worker(rank, world, port, pubs, causal, results, layout="contiguous", dtype=torch.float32, max_group=1):
     import torch.distributed as dist
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
         log = []
-        ex = _SharedMemoryExchange(rank, pubs, log)
-        hops = ring_plan(rank, world, 4 * world, causal, "contiguous")
+        ex = _SharedMemoryExchange(rank, pubs, log, max_group)
+        hops = ring_plan(rank, world, 4 * world, causal, layout)
         seen = []
         for call in range(3):
             # K carries (call, rank) so a hop that read a stale or foreign buffer shows it.
-            k = torch.full((1, 1, 4, 2), float(100 * call + rank))
+            k = torch.full((1, 1, 4, 2), float(100 * call + rank), dtype=dtype)
             v = -k
 
             def compute(hop, kk, vv):
+                # A merged launch sees its hops' shards side by side (4 rows each).
                 assert torch.equal(vv, -kk)
-                seen.append((call, hop.src, int(kk[0, 0, 0, 0])))
+                for j in range(kk.shape[2] // 4):
+                    seen.append((call, int(kk[0, 0, 4 * j, 0]) - 100 * call, int(kk[0, 0, 4 * j, 0])))
 
             # No barrier between calls besides the exchange's own: they alone
             # must keep a fast rank from overwriting what a slow rank still reads.
-            ring_loop(k, v, hops, compute, ex)
+            ring_loop(k, v, hops, compute, ex, merge=max_group > 1)
         results[rank] = (seen, log)
     finally:
         dist.destroy_process_group()
@@ -298,8 +315,48 @@ def test_ring_exchange_protocol_over_gloo(world, causal):
         want_src = [h.src for h in hops if h.problems]
         want = [(c, s, 100 * c + s) for c in range(3) for s in want_src]
         assert seen == want
-        pulls = [(h.src, i % 2) for i, h in enumerate(hops) if i > 0 and h.problems]
+        # One pull per live hop after the first, the two receive slots alternating.
+        pulls = [(s, g % 2) for g, s in enumerate(want_src) if g > 0]
         assert log == [e for _ in range(3) for e in [("pull", s, slot) for s, slot in pulls] + [("end",)]]
+
+
+def test_ring_exchange_protocol_with_merged_hops_over_gloo():
+    """The same protocol when the transport pulls two shards into one buffer:
+    on a 4-rank zigzag bf16 ring the middle (accumulate) hops of each rank go
+    out as one launch whose K/V holds both hops' shards side by side, pulled
+    with one pull_group; every hop's shard is still seen once per call, in hop
+    order."""
+    import socket
+
+    import torch.multiprocessing as mp
+    world = 4
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    pubs = [torch.zeros(2, 1, 1, 4, 2, dtype=torch.bfloat16).share_memory_() for _ in range(world)]
+    ctx = mp.get_context("spawn")
+    mgr = ctx.Manager()
+    results = mgr.dict()
+    procs = [ctx.Process(target=_gloo_worker, args=(r, world, port, pubs, True, results, "zigzag", torch.bfloat16, 2))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(120)
+        assert p.exitcode == 0
+    for r in range(world):
+        seen, log = results[r]
+        hops = ring_plan(r, world, 4 * world, True, "zigzag")
+        want_src = [h.src for h in hops if h.problems]
+        assert seen == [(c, s, 100 * c + s) for c in range(3) for s in want_src]
+        groups = launch_groups(hops, 4)
+        assert any(len(m) == 2 for m, _ in groups)
+        pulls = []
+        for g, (members, _) in enumerate(groups):
+            if g:
+                pulls.append(("pull", members[0].src, g % 2) if len(members) == 1 else
+                             ("pull", tuple(h.src for h in members), g % 2))
+        assert log == [e for _ in range(3) for e in pulls + [("end",)]]
 
 
 @pytest.mark.parametrize("bh,per", [(16, 2), (64, 19), (1, 1), (2, 2), (3, 2), (5, 1), (7, 4), (4, 8), (16, 16),
