@@ -372,12 +372,16 @@ class TimedExchange:
 
     def __init__(self, ex, phases):
         self.ex, self.phases, self.rank = ex, phases, ex.rank
+        self.max_group = getattr(ex, "max_group", 1)   # merged hops exactly as the untimed exchange runs them
 
     def publish(self, k, v):
         return self.phases.around("publish_copy_and_barrier", lambda: self.ex.publish(k, v))
 
     def pull(self, src, slot):
         return self.ex.pull(src, slot)
+
+    def pull_group(self, srcs, slot):
+        return self.ex.pull_group(srcs, slot)
 
     def ready(self, token):
         return self.ex.ready(token)
