@@ -149,11 +149,22 @@ def merge_hops(group: Sequence[RingHop], shard_len: int) -> RingHop:
     """One launch for consecutive accumulate hops whose shards sit side by side
     in one receive buffer: hop j's keys at rows [j*shard_len, (j+1)*shard_len)
     of every (batch, head) block. Their partial sums only add, so the launch
-    computes the same as the hops one after the other."""
-    problems = []
+    computes the same as the hops one after the other. A query segment's key
+    segments from all the hops go into as few problems as the kernel takes
+    (two key segments each, a partially visible one last), so its query pairs
+    run long items; a segment with more keys than one problem holds appears in
+    several problems, whose sums the persistent kernel adds."""
+    keys_of = {}
     for j, h in enumerate(group):
         for qr, ql, qp, keys in h.problems:
-            problems.append((qr, ql, qp, [(kr + j * shard_len, kl, kp) for kr, kl, kp in keys]))
+            keys_of.setdefault((qr, ql, qp), []).extend((kr + j * shard_len, kl, kp) for kr, kl, kp in keys)
+    problems = []
+    for (qr, ql, qp), keys in keys_of.items():
+        # Fully visible segments first: with causal masking only the second
+        # segment of a problem may be partially visible.
+        keys = sorted(keys, key=lambda k: k[2] + k[1] - 1 > qp)
+        for i in range(0, len(keys), 2):
+            problems.append((qr, ql, qp, keys[i:i + 2]))
     return RingHop(src=group[0].src, mode=group[0].mode, problems=problems)
 
 
