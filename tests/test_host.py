@@ -320,6 +320,42 @@ def test_ring_exchange_protocol_over_gloo(world, causal):
         assert log == [e for _ in range(3) for e in [("pull", s, slot) for s, slot in pulls] + [("end",)]]
 
 
+@pytest.mark.parametrize("world", [4, 6, 8])
+@pytest.mark.parametrize("layout", ["zigzag", "contiguous"])
+@pytest.mark.parametrize("causal", [False, True])
+def test_merged_hops_cover_the_same_pairs(world, layout, causal):
+    """A merged launch computes exactly the (query row, key) pairs of its member
+    hops: every key row of the merged problems, read in the side-by-side
+    receive buffer, is the key of the right shard at the right global position,
+    no pair appears twice, and each problem keeps the kernel's limits (at most
+    two key segments, a partially visible one last)."""
+    seq = 32 * 2 * world
+    for r in range(world):
+        hops = ring_plan(r, world, seq, causal, layout)
+        shard = seq // world
+        srcsegs = {s: local_segments(s, world, seq, layout) for s in range(world)}
+        groups = launch_groups(hops, shard)
+        assert [h.src for m, _ in groups for h in m] == [h.src for h in hops if h.problems]
+        for members, launched in groups:
+            assert len(launched.problems) <= 4
+            want, got = set(), []
+            for h in members:
+                for qr, ql, qp, keys in h.problems:
+                    for kr, kl, kp in keys:
+                        want |= {(qp + i, kp + j) for i in range(ql) for j in range(kl)}
+            for qr, ql, qp, keys in launched.problems:
+                assert 1 <= len(keys) <= 2
+                if causal and len(keys) == 2:
+                    assert keys[0][2] + keys[0][1] - 1 <= qp, "only the last key segment may be partial"
+                for kr, kl, kp in keys:
+                    j, row = divmod(kr, shard)
+                    src = members[j].src
+                    # rows [row, row + kl) of src's shard hold global positions [kp, kp + kl)
+                    assert any(r0 <= row and row + kl <= r0 + n and kp == p0 + row - r0 for r0, n, p0 in srcsegs[src])
+                    got += [(qp + i, kp + jj) for i in range(ql) for jj in range(kl)]
+            assert len(got) == len(set(got)) and set(got) == want
+
+
 def test_ring_exchange_protocol_with_merged_hops_over_gloo():
     """The same protocol when the transport pulls two shards into one buffer:
     on a 4-rank zigzag bf16 ring the middle (accumulate) hops of each rank go
