@@ -314,6 +314,11 @@ def run_ring(args, rank, world, peaks, traffic):
     per_launch_flops = flops / world / launches_per_step
     achieved = per_launch_flops / (launch_ms / 1e3) / 1e12
     tr = traffic.get("ring_n1" if world == 1 else f"ring_n{world}")
+    if tr is not None and world > 1:
+        # The capture is of one accumulate hop; a launch here carries
+        # live hops / launches of them on average (two middle hops merge), and
+        # the bytes of a hop's K/V, Q and accumulators scale with its count.
+        tr = tr * sum(1 for h in hops if h.problems) / launches_per_step
     res = {
         "value": value,
         "ms_per_step": ms / args.steps,
