@@ -323,8 +323,9 @@ def run_ring(args, rank, world, peaks, traffic):
         "value": value,
         "ms_per_step": ms / args.steps,
         "tok_per_s": RING["L"] * RING["B"] * args.steps / (ms / 1e3),
-        # One attention kernel per hop; the last hop of a ring call (FINALIZE)
-        # also launches its divide pass after the persistent accumulate kernel.
+        # One attention kernel per launch (a hop, or two merged middle hops);
+        # the last hop of a ring call (FINALIZE) also launches its divide pass
+        # after the persistent accumulate kernel.
         "gpu_launches": kt.count() + (args.steps if world > 1 else 0),
         "roofline": {"bound": "tensor", "kernel": "afa_tc_fwd_kernel<128>" if world == 1 else
                      "afa_tc_fwd_kernel<128> (first hop) / afa_tc_sk_kernel<128> (other hops)", "achieved": achieved,
