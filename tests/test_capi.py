@@ -82,6 +82,24 @@ def test_hop_argument_checks():
     assert rc == _lib.AFA_ERR_INVALID and b"o_acc" in lib.afa_last_error()
 
 
+def test_hop_shared_query_rows_only_where_pieces_add():
+    """Two problems over the same query rows (two ring hops in one launch) are
+    accepted only in AFA_HOP_ACCUMULATE on the tensor cores, whose persistent
+    kernel adds every piece with reductions; elsewhere the overlap is an
+    argument error found before any CUDA call."""
+    lib = _lib.load()
+    same_rows = (ctypes.c_int * 20)(0, 128, 0, 1, 0, 128, 0, 0, 0, 0,
+                                    0, 128, 0, 1, 128, 128, 128, 0, 0, 0)
+    for dtype, mode in ((_lib.AFA_F32, _lib.AFA_HOP_ACCUMULATE), (_lib.AFA_BF16, _lib.AFA_HOP_STORE),
+                        (_lib.AFA_BF16, _lib.AFA_HOP_FINALIZE)):
+        rc = lib.afa_fwd_hop(1, 1, 1, 1, 1, 1, None, 1, 1, 128, 256, 128, dtype, same_rows, 2, 0, mode, 0.5, None)
+        assert rc == _lib.AFA_ERR_INVALID and b"overlapping" in lib.afa_last_error()
+    # Accepted by the argument checks (the launch itself then needs a GPU).
+    rc = lib.afa_fwd_hop(1, 1, 1, 1, 1, None, None, 1, 1, 128, 256, 128, _lib.AFA_BF16, same_rows, 2, 0,
+                         _lib.AFA_HOP_ACCUMULATE, 0.5, None)
+    assert b"overlapping" not in lib.afa_last_error()
+
+
 def test_decode_workspace_query():
     lib = _lib.load()
     # batch 64 x 32 heads already fills the GPU: no split, no workspace
